@@ -21,10 +21,11 @@ ATTENTION_MEAN_ABS = 2.0 ** -16
 # in an early stage (the reference's own torch CPU sum is not correctly
 # rounded), and that flip propagates through the per-head norm, RoPE, the
 # softmax and the O projection, so per-element adjacency is meaningless after
-# the first stage.  Stated tolerance: max-abs <= 2^-7, mean-abs <= 2^-11 and
-# relative RMS error <= 2^-6 (the tensors are O(0.1..1)).
-E2E_MAX_ABS = 2.0 ** -7
-E2E_MEAN_ABS = 2.0 ** -11
+# the first stage.  Stated tolerance, relative to the expected tensor's own
+# scale: max-abs <= 2^-6 * max|expected| (two BF16 ulps at the largest
+# element), mean-abs <= 2^-8 * rms(expected), relative RMS error <= 2^-6.
+E2E_MAX_REL = 2.0 ** -6
+E2E_MEAN_REL = 2.0 ** -8
 E2E_REL_RMS = 2.0 ** -6
 
 
@@ -104,7 +105,9 @@ def assert_e2e_policy(actual, expected) -> Bf16Metrics:
     ef = bits_to_f32(e).astype(np.float64)
     diff = bits_to_f32(a).astype(np.float64) - ef
     rel = float(np.sqrt(np.mean(diff * diff)) / max(np.sqrt(np.mean(ef * ef)), 1e-30)) if ef.size else 0.0
-    assert m.max_abs <= E2E_MAX_ABS, str(m)
-    assert m.mean_abs <= E2E_MEAN_ABS, str(m)
+    scale_max = float(np.max(np.abs(ef), initial=0.0))
+    scale_rms = float(np.sqrt(np.mean(ef * ef))) if ef.size else 0.0
+    assert m.max_abs <= E2E_MAX_REL * scale_max, f"max-abs vs {scale_max:.3g}: {m}"
+    assert m.mean_abs <= E2E_MEAN_REL * scale_rms, f"mean-abs vs rms {scale_rms:.3g}: {m}"
     assert rel <= E2E_REL_RMS, f"relative rms error {rel:.3g}: {m}"
     return m
