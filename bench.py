@@ -1,0 +1,453 @@
+"""Benchmark: canonical NVFP4-W4A16 decoder-attention decode step on B200.
+
+Metric: decode tokens/s and us/step at B=1 (configs[0]:
+T=1, H=3072, Hq=24, Hkv=6, D=128, P=511, C=1024), HBM GB/s as % of peak.
+
+A "step" is one forward of one decode token through the fused path: three
+kernels (fused QKV+norms+RoPE+append, split-KV attention, O projection)
+chained by programmatic dependent launch.  Inputs are resident in HBM; steps
+rotate over R replicas of weights + caches + activations whose total exceeds
+2x the 126 MB L2, so every step streams its 14.9 MB from HBM.  The timed loop
+replays a CUDA graph of R steps.
+
+Multi-GPU (torchrun, one process per GPU): every rank decodes its own
+independent sequence (weak scaling, no collective on the data path); value is
+the tokens of all ranks over the max-over-ranks device time.
+
+--impl reference times the reference's CPU path (the numpy restatement of
+reference/decoder_attention_nvfp4.py in oracle/; the Python reference itself
+cannot travel to the GPU box) on the host cores, on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "cuda-nvfp4-decoder-attention_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "decode tokens/s (B=1 canonical decode step)"
+UNIT = "tokens/s"
+WORKLOAD = ("configs[0] canonical decode: B=1 T=1 H=3072 Hq=24 Hkv=6 D=128 P=511 C=1024, "
+            "NVFP4 W4A16 Q/K/V/O, BF16 caches")
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------- algorithmic bytes
+def step_bytes(shape) -> dict:
+    """Algorithmic (each byte once) HBM traffic of one decode step."""
+    h, d, hkv, hq = shape.hidden, shape.head_dim, shape.kv_heads, shape.q_heads
+    m = shape.batch * shape.tokens
+    kvw = hkv * d
+    w = lambda n, k: n * (k // 2 + k // 16) + 4  # noqa: E731
+    w_qkv = w(h, h) + 2 * w(kvw, h)
+    w_o = w(h, h)
+    s = shape.past(0) + shape.tokens
+    kv_read = shape.batch * s * 2 * kvw * 2
+    append = m * 2 * kvw * 2
+    act = m * h * 2
+    norms = h * 2 + 2 * d * 2
+    qkv = w_qkv + act + norms + m * hq * d * 2 + append  # x, gains, q out, K/V append
+    attn = kv_read + 2 * m * hq * d * 2  # caches, q in, context out
+    o = w_o + 2 * act  # weights, context in, output out
+    total = w_qkv + w_o + kv_read + append + 2 * act + norms
+    return {"qkv": qkv, "attention": attn, "o_proj": o, "step": total}
+
+
+def measured_peak_gbs() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- GPU arm
+class Replica:
+    def __init__(self, inp, ws, capi):
+        dev = "cuda"
+        self.x = inp.x.to(dev)
+        self.g_in = inp.input_norm_weight.to(dev)
+        self.g_q = inp.q_norm_weight.to(dev)
+        self.g_k = inp.k_norm_weight.to(dev)
+        self.kc = inp.k_cache.to(dev)
+        self.vc = inp.v_cache.to(dev)
+        self.ws = {k: w.to(dev) for k, w in ws.items()}
+        self.out = torch.empty_like(self.x)
+        self.q_rope = torch.empty((1, 1, 24, 128), dtype=torch.bfloat16, device=dev)
+        self.ctx = torch.empty_like(self.q_rope)
+        self.fw = capi.Forward(self.x, self.g_in, self.ws["q"], self.ws["k"], self.ws["v"], self.g_q, self.g_k,
+                               self.ws["o"], self.kc, self.vc, self.out, past_length=511)
+        lib = capi.load()
+        self.attn_ws_bytes = lib.nvfp4da_gqa_attention_workspace_size(1, 1, 24, 6, 128, 511)
+        self.attn_ws = torch.empty(max(1, self.attn_ws_bytes), dtype=torch.uint8, device=dev)
+
+
+def timed_graph(fn_list, reps: int, stream) -> float:
+    """Capture fn_list (one call each) into a graph, replay `reps` times; ms total."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for fn in fn_list:
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(reps):
+            g.replay()
+        end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def run_gpu(args) -> None:
+    world, rank, local = dist_setup()
+    import cuda_primitives  # noqa: F401  (loads the operator library; fails loudly if unbuilt)
+    import decoder_attention_cuda
+    import nvfp4da_capi as capi
+    import synthetic
+    from nvfp4_tensor import NVFP4Tensor
+
+    capi.load()
+    shape = synthetic.CANONICAL
+    inp = synthetic.make_decode_inputs(shape, seed=0)
+    ws = {}
+    for k, w in inp.weights_fp32.items():
+        packed, scales, gamma = capi.quantize(w.cuda())
+        ws[k] = NVFP4Tensor(packed, scales, gamma, tuple(w.shape))
+    nbytes = step_bytes(shape)
+    replica_bytes = nbytes["step"] + 2 * inp.k_cache.numel() * 2
+    n_rep = max(2, math.ceil(2 * L2_BYTES / replica_bytes))
+    reps = [Replica(inp, ws, capi) for _ in range(n_rep)]
+    stream = torch.cuda.Stream()
+
+    # warm-up (untimed)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            reps[i % n_rep].fw.run(stream)
+    torch.cuda.synchronize()
+
+    # ---- timed region: exactly K steps, graph replays of n_rep steps (+ a tail graph)
+    k = args.steps
+    full, tail = divmod(k, n_rep)
+    step_fns = [(lambda r=r: r.fw.run(stream)) for r in reps]
+    g_full = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_full, stream=stream):
+        for fn in step_fns:
+            fn()
+    g_tail = None
+    if tail:
+        g_tail = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_tail, stream=stream):
+            for fn in step_fns[:tail]:
+                fn()
+    g_full.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)  # let the sampler start before the timed region
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(full):
+            g_full.replay()
+        if g_tail is not None:
+            g_tail.replay()
+        end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    tokens = world * shape.batch * shape.tokens * k
+    value = tokens / (ms / 1e3)
+    ms_per_step = ms / k
+
+    # ---- per-kernel device time in isolation (same rotation, graphs of n_rep launches)
+    lib = capi.load()
+
+    def attn_call(r):
+        st = lib.nvfp4da_gqa_attention_cached(r.q_rope.data_ptr(), r.kc.data_ptr(), r.vc.data_ptr(),
+                                              r.ctx.data_ptr(), 1, 1, 24, 6, 1024, 128, 511, None, 511,
+                                              r.attn_ws.data_ptr(), r.attn_ws_bytes,
+                                              torch.cuda.current_stream().cuda_stream)
+        assert st == 0, lib.nvfp4da_last_error()
+
+    reps_k = max(20, min(2000, k // n_rep))
+    kern_ms = {
+        "qkv": timed_graph([(lambda r=r: r.fw.run_qkv(r.q_rope, stream)) for r in reps], reps_k, stream),
+        "attention": timed_graph([(lambda r=r: attn_call(r)) for r in reps], reps_k, stream),
+        "o_proj": timed_graph([(lambda r=r: capi.w4a16_linear(r.ctx.view(1, 3072), r.ws["o"],
+                                                              r.out.view(1, 3072), stream)) for r in reps],
+                              reps_k, stream),
+    }
+    per_launch_us = {n: v * 1e3 / (reps_k * n_rep) for n, v in kern_ms.items()}
+    peak, peak_src = measured_peak_gbs()
+    kernels = {n: {"us": round(per_launch_us[n], 3), "bytes": nbytes[n],
+                   "gbs": round(nbytes[n] / (per_launch_us[n] * 1e-6) / 1e9, 1)} for n in kern_ms}
+    qkv_gbs = nbytes["qkv"] / (per_launch_us["qkv"] * 1e-6) / 1e9
+    step_gbs = nbytes["step"] / (ms_per_step * 1e-3) / 1e9
+
+    # ---- end to end through the drop-in Python API with host buffers
+    e2e = run_e2e(args, reps, decoder_attention_cuda, stream, world)
+
+    if rank != 0:
+        _finish(world)
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": k,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "us_per_step": round(ms_per_step * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; configs[0] distributions, random-init NVFP4 weights)",
+        "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": 512,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": f"inputs larger than L2: {n_rep} rotating weight+cache replicas "
+                         f"({n_rep * replica_bytes / 2**20:.0f} MiB > 2 x 126 MB L2)",
+                   "timing": f"CUDA graph of {n_rep} PDL-chained steps replayed, CUDA events"},
+        "roofline": {"bound": "hbm", "kernel": "qkv_fused (input norm + W4A16 QKV + head norm + RoPE + append)",
+                     "achieved": round(qkv_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(qkv_gbs / peak, 4), "peak_source": peak_src,
+                     "traffic": None,
+                     "bytes_per_launch": nbytes["qkv"],
+                     "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
+                     "step_bytes": nbytes["step"]},
+        "kernels": kernels,
+        "e2e": e2e,
+        "gpu_launches": 3 * k,
+        "clocks": clk,
+    }
+    if world == 1 and not args.skip_cpu:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    _finish(world)
+
+
+def run_e2e(args, reps, dac, stream, world) -> dict:
+    """Same metric through cuda_decoder_attention_forward_ with pinned host
+    input copied in and the output copied out every step (inside the timing)."""
+    n = max(10, min(args.steps, args.e2e_steps))
+    x_host = [r.x.cpu().pin_memory() for r in reps]
+    out_host = torch.empty((1, 1, 3072), dtype=torch.bfloat16).pin_memory()
+
+    def step(i):
+        r = reps[i % len(reps)]
+        r.x.copy_(x_host[i % len(reps)], non_blocking=True)
+        y = dac.cuda_decoder_attention_forward_(r.x, r.g_in, r.ws["q"], r.ws["k"], r.ws["v"], r.g_q, r.g_k,
+                                                r.ws["o"], r.kc, r.vc, 511)
+        out_host.copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(10):
+            step(i)
+        torch.cuda.synchronize()
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(n):
+            step(i)
+        end.record(stream)
+    end.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    return {"value": round(world * n / (ms / 1e3), 1), "unit": UNIT, "steps": n,
+            "h2d_bytes_per_step": 3072 * 2, "d2h_bytes_per_step": 3072 * 2,
+            "path": "decoder_attention_cuda.cuda_decoder_attention_forward_ (drop-in Python op), "
+                    "pinned host x in, output out, per step"}
+
+
+def _finish(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- CPU path (reference arm / cpu_baseline)
+def _oracle_inputs():
+    sys.path.insert(0, str(ROOT))
+    import oracle
+    import synthetic
+
+    inp = synthetic.make_decode_inputs(synthetic.CANONICAL, seed=0)
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+    qw = {k: oracle.quantize(v.numpy()) for k, v in inp.weights_fp32.items()}
+    return oracle, (bits(inp.x), bits(inp.input_norm_weight), qw, bits(inp.q_norm_weight),
+                    bits(inp.k_norm_weight), bits(inp.k_cache), bits(inp.v_cache))
+
+
+def cpu_rate(seconds: float, max_steps: int | None = None) -> dict:
+    """Decode steps of the CPU restatement, one independent sequence per host
+    thread (numpy releases the GIL in its kernels), for about `seconds`."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    oracle, (x, g_in, qw, g_q, g_k, kc, vc) = _oracle_inputs()
+    threads = os.cpu_count() or 1
+    deadline = time.perf_counter() + seconds
+    counts = [0] * threads
+
+    def worker(i):
+        kci, vci = kc.copy(), vc.copy()
+        while time.perf_counter() < deadline and (max_steps is None or counts[i] < max_steps):
+            oracle.decoder_attention_nvfp4(x, g_in, qw["q"], qw["k"], qw["v"], g_q, g_k, qw["o"], kci, vci, 511)
+            counts[i] += 1
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(worker, range(threads)))
+    wall = time.perf_counter() - t0
+    steps = sum(counts)
+    return {"value": round(steps / wall, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} canonical decode steps of oracle/ (numpy restatement of "
+                      f"reference/decoder_attention_nvfp4.py), {threads} threads x independent sequences, "
+                      f"{wall:.1f} s wall"}
+
+
+def cpu_baseline(seconds: float) -> dict:
+    return cpu_rate(seconds)
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    # warm-up: one untimed step per thread, then a bounded timed sample.
+    cpu_rate(1.0, max_steps=1)
+    res = cpu_rate(args.cpu_seconds)
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 / res["value"], 3) if res["value"] else None,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded; configs[0] distributions)", "impl": "reference",
+        "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": 512, "parallelism": "host threads"},
+        "cpu_baseline": res,
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "each step is a bounded sample: the timed run lasts about --cpu-seconds regardless of --steps",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=160000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

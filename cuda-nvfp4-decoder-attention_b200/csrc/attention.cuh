@@ -1,0 +1,284 @@
+// Split-KV flash-decoding causal GQA over the physical BF16 cache [B, Hkv, C, D].
+//
+// Semantics (reference/decoder_attention.py:273-381, src/gqa_attention_cached.cu):
+//   query head h reads KV head h / (Hq/Hkv); token t of sequence b sees keys
+//   j <= P_b + t; score = FP32(q . k) * FP32(1/sqrt(D)); softmax in FP32;
+//   context = BF16(sum_j p_j v_j).  K/V rows are addressed with the physical
+//   capacity C as the head stride; slots beyond P_b + t are never read.
+//
+// Work decomposition: one CTA per (split, kv head x head group, b*T + t).  The
+// CTA's GH query heads share every K/V row it loads.  Four warps walk the
+// split's positions in chunks of NPOS = 32/GH rows; lane l holds elements
+// [l*EPL, l*EPL+EPL) of q, k and v.  Per chunk the NPOS x GH partial dot
+// products are summed across lanes with a butterfly reduce-scatter (31
+// shuffles), after which lane l owns the score of (row l/GH, head l%GH).
+// Softmax is online (running max and sum per head, FP32).  Partial (m, l, o)
+// of every split go to the workspace; the last CTA of a (b, t, head group) to
+// finish — detected with an atomic counter, no waiting — combines them with
+// the log-sum-exp rule and writes BF16 context.  No score or probability
+// tensor is materialised.
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+
+namespace nvfp4da {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * kWarp;
+
+struct AttnParams {
+  const uint16_t* q;        // [B, T, Hq, D]
+  const uint16_t* k_cache;  // [B, Hkv, C, D]
+  const uint16_t* v_cache;
+  uint16_t* ctx;  // [B, T, Hq, D]
+  int64_t batch, tokens, q_heads, kv_heads, capacity, head_dim;
+  int64_t past_length;          // used when past_lengths == nullptr
+  const int64_t* past_lengths;  // optional device [B]
+  int64_t split_len;            // positions per split (multiple of 32)
+  int splits;
+  int head_groups;  // (Hq/Hkv) / GH
+  float scale;      // FP32(1/sqrt(D))
+  float* partials;  // [B*T*Hq][splits][D + 2]  (o[D], m, l)
+  unsigned* counters;  // [B*T*Hkv*head_groups], zero on entry, left zero on exit
+  int pdl;
+};
+
+template <int EPL>
+__device__ __forceinline__ void load_row(const uint16_t* row, int lane, int64_t d, float (&out)[EPL]) {
+  if (lane * EPL < d) {
+    const uint16_t* p = row + lane * EPL;
+    if constexpr (EPL == 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        out[2 * i] = __uint_as_float(w[i] << 16);
+        out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    } else if constexpr (EPL == 4) {
+      const uint2 v = *reinterpret_cast<const uint2*>(p);
+      out[0] = __uint_as_float(v.x << 16);
+      out[1] = __uint_as_float(v.x & 0xffff0000u);
+      out[2] = __uint_as_float(v.y << 16);
+      out[3] = __uint_as_float(v.y & 0xffff0000u);
+    } else if constexpr (EPL == 2) {
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+      out[0] = __uint_as_float(v << 16);
+      out[1] = __uint_as_float(v & 0xffff0000u);
+    } else {
+      out[0] = bf16_bits_to_f32(*p);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = 0.0f;
+  }
+}
+
+// Butterfly reduce-scatter of 32 per-lane values: afterwards lane l holds the
+// sum over all lanes of v[l].
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+      const float send = upper ? v[i] : v[i + s];
+      const float keep = upper ? v[i + s] : v[i];
+      v[i] = keep + __shfl_xor_sync(kFull, send, s);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ int64_t seq_past(const AttnParams& p, int64_t b) {
+  return p.past_lengths ? p.past_lengths[b] : p.past_length;
+}
+
+template <int EPL, int GH>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) {
+  constexpr int NPOS = 32 / GH;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / p.head_groups;
+  const int hg = blockIdx.y % p.head_groups;
+  const int64_t bt = blockIdx.z;
+  const int64_t b = bt / p.tokens;
+  const int64_t t = bt % p.tokens;
+  const int64_t d = p.head_dim;
+  const int64_t group = p.q_heads / p.kv_heads;
+  const int64_t h0 = static_cast<int64_t>(kvh) * group + static_cast<int64_t>(hg) * GH;
+
+  if (p.pdl) {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+
+  const int64_t visible = seq_past(p, b) + t + 1;  // keys 0 .. P_b + t
+  const int64_t s0 = static_cast<int64_t>(split) * p.split_len;
+  int64_t s1 = s0 + p.split_len;
+  if (s1 > visible) s1 = visible;
+
+  // q for GH heads, this lane's slice.
+  float q[GH][EPL];
+#pragma unroll
+  for (int g = 0; g < GH; ++g) load_row<EPL>(p.q + ((bt * p.q_heads) + h0 + g) * d, lane, d, q[g]);
+
+  const uint16_t* kbase = p.k_cache + (b * p.kv_heads + kvh) * p.capacity * d;
+  const uint16_t* vbase = p.v_cache + (b * p.kv_heads + kvh) * p.capacity * d;
+
+  float m_run[GH], l_run[GH], acc[GH][EPL];
+#pragma unroll
+  for (int g = 0; g < GH; ++g) {
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[g][e] = 0.0f;
+  }
+
+  for (int64_t c0 = s0 + static_cast<int64_t>(warp) * NPOS; c0 < s1; c0 += kAttnWarps * NPOS) {
+    float kr[NPOS][EPL], vr[NPOS][EPL];
+#pragma unroll
+    for (int j = 0; j < NPOS; ++j) {
+      const int64_t pos = c0 + j;
+      if (pos < s1) {
+        load_row<EPL>(kbase + pos * d, lane, d, kr[j]);
+        load_row<EPL>(vbase + pos * d, lane, d, vr[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) kr[j][e] = vr[j][e] = 0.0f;
+      }
+    }
+    float dots[32];
+#pragma unroll
+    for (int j = 0; j < NPOS; ++j)
+#pragma unroll
+      for (int g = 0; g < GH; ++g) {
+        float s = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) s = fmaf(q[g][e], kr[j][e], s);
+        dots[j * GH + g] = s;
+      }
+    const float dot = reduce_scatter32(dots, lane);
+    const int my_j = lane / GH;
+    const int my_g = lane % GH;
+    const bool valid = (c0 + my_j) < s1;
+    const float score = valid ? __fmul_rn(dot, p.scale) : -INFINITY;
+    // chunk max per head (lanes sharing my_g)
+    float cmax = score;
+#pragma unroll
+    for (int o = GH; o < 32; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(kFull, cmax, o));
+    float m_old_mine = m_run[0];
+#pragma unroll
+    for (int g = 1; g < GH; ++g)
+      if (my_g == g) m_old_mine = m_run[g];
+    const float m_new_mine = fmaxf(m_old_mine, cmax);  // finite: chunk has >= 1 valid row
+    const float pexp = valid ? expf(score - m_new_mine) : 0.0f;
+    float psum = pexp;
+#pragma unroll
+    for (int o = GH; o < 32; o <<= 1) psum += __shfl_xor_sync(kFull, psum, o);
+    const float alpha_mine = (m_old_mine == -INFINITY) ? 0.0f : expf(m_old_mine - m_new_mine);
+#pragma unroll
+    for (int g = 0; g < GH; ++g) {
+      const float alpha = __shfl_sync(kFull, alpha_mine, g);
+      const float mnew = __shfl_sync(kFull, m_new_mine, g);
+      const float ps = __shfl_sync(kFull, psum, g);
+      m_run[g] = mnew;
+      l_run[g] = fmaf(l_run[g], alpha, ps);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[g][e] *= alpha;
+    }
+#pragma unroll
+    for (int j = 0; j < NPOS; ++j)
+#pragma unroll
+      for (int g = 0; g < GH; ++g) {
+        const float pj = __shfl_sync(kFull, pexp, j * GH + g);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[g][e] = fmaf(pj, vr[j][e], acc[g][e]);
+      }
+  }
+
+  // ---- combine the four warps of this CTA
+  __shared__ float sm_m[kAttnWarps][GH], sm_l[kAttnWarps][GH];
+  __shared__ float sm_o[kAttnWarps][GH][32 * EPL];
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < GH; ++g) {
+      sm_m[warp][g] = m_run[g];
+      sm_l[warp][g] = l_run[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GH; ++g)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) sm_o[warp][g][lane * EPL + e] = acc[g][e];
+  __syncthreads();
+
+  // thread i handles element i of head g for i < d (loop over heads)
+  float* part_base = p.partials;
+  const bool single = (p.splits == 1);
+  for (int idx = threadIdx.x; idx < GH * 32 * EPL; idx += kAttnThreads) {
+    const int g = idx / (32 * EPL);
+    const int e = idx % (32 * EPL);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, sm_m[w][g]);
+    float l = 0.0f, o = 0.0f;
+    if (mx != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = (sm_m[w][g] == -INFINITY) ? 0.0f : expf(sm_m[w][g] - mx);
+        l = fmaf(sm_l[w][g], f, l);
+        o = fmaf(sm_o[w][g][e], f, o);
+      }
+    }
+    if (e >= d) continue;
+    const int64_t row = bt * p.q_heads + h0 + g;
+    if (single) {
+      p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
+    } else {
+      float* dst = part_base + (row * p.splits + split) * (d + 2);
+      dst[e] = o;
+      if (e == 0) {
+        dst[d] = mx;
+        dst[d + 1] = l;
+      }
+    }
+  }
+  if (single) return;
+
+  // ---- last CTA of this (b, t, head group) combines all splits
+  __shared__ unsigned s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned idx = static_cast<unsigned>(bt * (p.kv_heads * p.head_groups) + blockIdx.y);
+    const unsigned prev = atomicAdd(&p.counters[idx], 1u);
+    s_last = (prev == static_cast<unsigned>(p.splits - 1)) ? 1u : 0u;
+    if (s_last) p.counters[idx] = 0u;  // leave zero for the next launch
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < GH * d; idx += kAttnThreads) {
+    const int g = static_cast<int>(idx / d);
+    const int64_t e = idx % d;
+    const int64_t row = bt * p.q_heads + h0 + g;
+    const float* src = part_base + row * p.splits * (d + 2);
+    float mx = -INFINITY;
+    for (int s = 0; s < p.splits; ++s) mx = fmaxf(mx, __ldcg(src + s * (d + 2) + d));
+    float l = 0.0f, o = 0.0f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float ms = __ldcg(src + s * (d + 2) + d);
+      if (ms == -INFINITY) continue;
+      const float f = expf(ms - mx);
+      l = fmaf(__ldcg(src + s * (d + 2) + d + 1), f, l);
+      o = fmaf(__ldcg(src + s * (d + 2) + e), f, o);
+    }
+    p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
+  }
+}
+
+}  // namespace nvfp4da

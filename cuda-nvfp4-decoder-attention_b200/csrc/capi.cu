@@ -1,0 +1,693 @@
+// C ABI of libnvfp4da.so: validation, launch planning and kernel launches.
+// Declarations and reference citations: include/nvfp4_decoder_attention.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <string>
+
+#include "../../include/nvfp4_decoder_attention.h"
+#include "attention.cuh"
+#include "elementwise.cuh"
+#include "gemv_kernel.cuh"
+#include "qkv_fused.cuh"
+
+namespace nvfp4da {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(NVFP4DA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define NVFP4DA_CHECK_LAUNCH(what)                       \
+  do {                                                   \
+    cudaError_t e_ = cudaGetLastError();                 \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what);   \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+constexpr uint32_t kMaxDynSmem = 227 * 1024;
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int sm_count() {
+  static int cached[kMaxDevices] = {0};
+  const int dev = current_device();
+  if (dev < kMaxDevices && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < kMaxDevices) cached[dev] = n;
+  return n;
+}
+
+// Raise the dynamic shared-memory limit of `fn` on the current device once.
+template <typename F>
+cudaError_t ensure_smem(F* fn, uint32_t bytes) {
+  static uint32_t set_bytes[kMaxDevices] = {0};
+  const int dev = current_device();
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  if (dev < kMaxDevices && set_bytes[dev] >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess && dev < kMaxDevices) set_bytes[dev] = bytes;
+  return e;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int check_weight(const nvfp4da_weight* w, const char* name) {
+  if (!w) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+  if (!w->packed_values || !w->block_scales || !w->global_decode_scale)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "%s has a NULL field", name);
+  if (w->rows <= 0 || w->cols <= 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "%s dimensions must be positive", name);
+  if (w->cols < 16 || w->cols % 16 != 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "logical K must be a positive multiple of 16, got %lld",
+                static_cast<long long>(w->cols));
+  return NVFP4DA_OK;
+}
+
+// ---------------------------------------------------------------- GEMV plan
+struct GemvPlan {
+  int rpw, mg;
+  uint32_t smem;
+  int64_t ctas;
+};
+
+bool plan_gemv(int64_t m, int64_t n, int64_t k, GemvPlan& pl) {
+  const int sms = sm_count();
+  int rpw = 1;
+  for (int r : {4, 2}) {
+    if (ceil_div(n, kGemvWarps * r) >= sms) {
+      rpw = r;
+      break;
+    }
+  }
+  int mg = m <= 1 ? 1 : (m == 2 ? 2 : 4);
+  for (;;) {
+    const uint32_t bytes = gemv_layout(kGemvWarps * rpw, k, mg).total();
+    if (bytes <= kMaxDynSmem) {
+      pl = {rpw, mg, bytes, ceil_div(n, kGemvWarps * rpw)};
+      return true;
+    }
+    if (mg > 1) mg >>= 1;
+    else if (rpw > 1) rpw >>= 1;
+    else return false;
+  }
+}
+
+template <int RPW, int MG>
+cudaError_t launch_gemv_t(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+  auto* k = w4a16_gemv_kernel<RPW, MG>;
+  cudaError_t e = ensure_smem(k, pl.smem);
+  if (e != cudaSuccess) return e;
+  return launch(k, dim3(static_cast<unsigned>(pl.ctas)), dim3(kGemvThreads), pl.smem, s, pdl, p);
+}
+
+cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+#define NVFP4DA_GEMV_CASE(R, M) \
+  if (pl.rpw == R && pl.mg == M) return launch_gemv_t<R, M>(p, pl, s, pdl);
+  NVFP4DA_GEMV_CASE(1, 1)
+  NVFP4DA_GEMV_CASE(1, 2)
+  NVFP4DA_GEMV_CASE(1, 4)
+  NVFP4DA_GEMV_CASE(2, 1)
+  NVFP4DA_GEMV_CASE(2, 2)
+  NVFP4DA_GEMV_CASE(2, 4)
+  NVFP4DA_GEMV_CASE(4, 1)
+  NVFP4DA_GEMV_CASE(4, 2)
+  NVFP4DA_GEMV_CASE(4, 4)
+#undef NVFP4DA_GEMV_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
+int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s, bool pdl) {
+  GemvPlan pl;
+  if (!plan_gemv(m, w.rows, w.cols, pl))
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "K=%lld is too large for the shared-memory GEMV", static_cast<long long>(w.cols));
+  if (pl.ctas > std::numeric_limits<int32_t>::max())
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "N is too large for a one-dimensional grid");
+  GemvParams p{x, m, w.packed_values, w.block_scales, w.global_decode_scale, y, w.rows, w.cols, nullptr, pdl ? 1 : 0};
+  cudaError_t e = launch_gemv(p, pl, s, pdl);
+  if (e != cudaSuccess) return cuda_fail(e, "w4a16 gemv launch");
+  return NVFP4DA_OK;
+}
+
+// ---------------------------------------------------------------- attention plan
+struct AttnPlan {
+  int epl, gh, head_groups, splits;
+  int64_t split_len;
+  size_t partial_bytes, counter_bytes;
+};
+
+bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                    int64_t max_past, AttnPlan& pl) {
+  if (head_dim <= 0 || head_dim > 256) return false;
+  int epl = head_dim <= 32 ? 1 : head_dim <= 64 ? 2 : head_dim <= 128 ? 4 : 8;
+  if (head_dim % epl != 0) return false;
+  const int64_t group = q_heads / kv_heads;
+  int gh = 1;
+  for (int g : {8, 4, 2}) {
+    if (group % g == 0) {
+      gh = g;
+      break;
+    }
+  }
+  const int64_t ng = group / gh;
+  const int64_t chunk = kAttnWarps * (32 / gh);
+  const int64_t visible = max_past + tokens;
+  const int64_t base = batch * tokens * kv_heads * ng;
+  int64_t splits = ceil_div(8LL * sm_count(), base);
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, ceil_div(visible, chunk)));
+  int64_t split_len = ceil_div(ceil_div(visible, splits), chunk) * chunk;
+  splits = ceil_div(visible, split_len);
+  if (splits > 65535) {
+    splits = 65535;
+    split_len = ceil_div(ceil_div(visible, splits), chunk) * chunk;
+    splits = ceil_div(visible, split_len);
+  }
+  pl.epl = epl;
+  pl.gh = gh;
+  pl.head_groups = static_cast<int>(ng);
+  pl.splits = static_cast<int>(splits);
+  pl.split_len = split_len;
+  pl.partial_bytes = splits > 1 ? align_up(static_cast<size_t>(batch * tokens * q_heads) * splits * (head_dim + 2) * 4, 256) : 0;
+  pl.counter_bytes = splits > 1 ? align_up(static_cast<size_t>(base) * 4, 256) : 0;
+  return true;
+}
+
+template <int EPL, int GH>
+cudaError_t launch_attn_t(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl) {
+  return launch(attn_split_kernel<EPL, GH>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+}
+
+cudaError_t launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s, bool pdl) {
+  const dim3 grid(static_cast<unsigned>(pl.splits), static_cast<unsigned>(p.kv_heads * pl.head_groups),
+                  static_cast<unsigned>(p.batch * p.tokens));
+#define NVFP4DA_ATTN_CASE(E, G) \
+  if (pl.epl == E && pl.gh == G) return launch_attn_t<E, G>(p, grid, s, pdl);
+  NVFP4DA_ATTN_CASE(1, 1)
+  NVFP4DA_ATTN_CASE(1, 2)
+  NVFP4DA_ATTN_CASE(1, 4)
+  NVFP4DA_ATTN_CASE(1, 8)
+  NVFP4DA_ATTN_CASE(2, 1)
+  NVFP4DA_ATTN_CASE(2, 2)
+  NVFP4DA_ATTN_CASE(2, 4)
+  NVFP4DA_ATTN_CASE(2, 8)
+  NVFP4DA_ATTN_CASE(4, 1)
+  NVFP4DA_ATTN_CASE(4, 2)
+  NVFP4DA_ATTN_CASE(4, 4)
+  NVFP4DA_ATTN_CASE(4, 8)
+  NVFP4DA_ATTN_CASE(8, 1)
+  NVFP4DA_ATTN_CASE(8, 2)
+  NVFP4DA_ATTN_CASE(8, 4)
+  NVFP4DA_ATTN_CASE(8, 8)
+#undef NVFP4DA_ATTN_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
+int check_attention_dims(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t capacity,
+                         int64_t head_dim, int64_t max_past) {
+  if (batch <= 0 || tokens <= 0 || q_heads <= 0 || kv_heads <= 0 || capacity <= 0 || head_dim <= 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "attention dimensions must all be positive");
+  if (q_heads % kv_heads != 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "number of query heads must be divisible by number of KV heads");
+  if (max_past < 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "past_length must be nonnegative");
+  if (max_past > std::numeric_limits<int64_t>::max() - tokens)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "past_length + current token count overflows int64");
+  if (max_past + tokens > capacity)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "past_length + current token count exceeds cache capacity (%lld > %lld)",
+                static_cast<long long>(max_past + tokens), static_cast<long long>(capacity));
+  if (batch * tokens > 65535 || kv_heads * q_heads > 65535)
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "B*T and Hq*Hkv must each be at most 65535");
+  return NVFP4DA_OK;
+}
+
+int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* ctx, int64_t batch,
+                  int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t capacity, int64_t head_dim,
+                  int64_t past_length, const int64_t* past_lengths, int64_t max_past, void* ws, size_t ws_bytes,
+                  cudaStream_t s, bool pdl, bool clear_counters) {
+  AttnPlan pl;
+  if (!plan_attention(batch, tokens, q_heads, kv_heads, head_dim, max_past, pl))
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "head_dim %lld is not supported (need head_dim <= 256 and divisible by "
+                "its per-lane vector width)", static_cast<long long>(head_dim));
+  if (pl.partial_bytes + pl.counter_bytes > ws_bytes || (pl.splits > 1 && !ws))
+    return fail(NVFP4DA_ERR_WORKSPACE, "attention workspace too small (%zu < %zu bytes)", ws_bytes,
+                pl.partial_bytes + pl.counter_bytes);
+  AttnParams p{};
+  p.q = q;
+  p.k_cache = kc;
+  p.v_cache = vc;
+  p.ctx = ctx;
+  p.batch = batch;
+  p.tokens = tokens;
+  p.q_heads = q_heads;
+  p.kv_heads = kv_heads;
+  p.capacity = capacity;
+  p.head_dim = head_dim;
+  p.past_length = past_length;
+  p.past_lengths = past_lengths;
+  p.split_len = pl.split_len;
+  p.splits = pl.splits;
+  p.head_groups = pl.head_groups;
+  p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)));
+  p.partials = pl.splits > 1 ? static_cast<float*>(ws) : nullptr;
+  p.counters = pl.splits > 1 ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pl.partial_bytes) : nullptr;
+  p.pdl = pdl ? 1 : 0;
+  if (clear_counters && pl.splits > 1) {
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, pl.counter_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "attention counter clear");
+  }
+  cudaError_t e = launch_attn(p, pl, s, pdl);
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return NVFP4DA_OK;
+}
+
+// ---------------------------------------------------------------- fused QKV plan
+struct QkvPlan {
+  int rpw, mg;
+  uint32_t smem;
+};
+
+bool plan_qkv(int64_t m, int64_t hidden, int64_t head_dim, QkvPlan& pl) {
+  if (head_dim % 32 != 0 || head_dim > kMaxHeadDim) return false;
+  const int rpw = static_cast<int>(head_dim / 32);
+  if (rpw != 1 && rpw != 2 && rpw != 4 && rpw != 8) return false;
+  int mg = m <= 1 ? 1 : (m == 2 ? 2 : 4);
+  for (;;) {
+    const uint32_t bytes = gemv_layout(kGemvWarps * rpw, hidden, mg).total();
+    if (bytes <= kMaxDynSmem - 8 * 1024) {
+      pl = {rpw, mg, bytes};
+      return true;
+    }
+    if (mg == 1) return false;
+    mg >>= 1;
+  }
+}
+
+template <int RPW, int MG>
+cudaError_t launch_qkv_t(const QkvParams& p, const QkvPlan& pl, int64_t units, cudaStream_t s, bool pdl) {
+  auto* k = qkv_fused_kernel<RPW, MG>;
+  cudaError_t e = ensure_smem(k, pl.smem);
+  if (e != cudaSuccess) return e;
+  return launch(k, dim3(static_cast<unsigned>(units * kQkvCluster)), dim3(kGemvThreads), pl.smem, s, pdl, p);
+}
+
+cudaError_t launch_qkv(const QkvParams& p, const QkvPlan& pl, int64_t units, cudaStream_t s, bool pdl) {
+#define NVFP4DA_QKV_CASE(R, M) \
+  if (pl.rpw == R && pl.mg == M) return launch_qkv_t<R, M>(p, pl, units, s, pdl);
+  NVFP4DA_QKV_CASE(1, 1)
+  NVFP4DA_QKV_CASE(1, 2)
+  NVFP4DA_QKV_CASE(1, 4)
+  NVFP4DA_QKV_CASE(2, 1)
+  NVFP4DA_QKV_CASE(2, 2)
+  NVFP4DA_QKV_CASE(2, 4)
+  NVFP4DA_QKV_CASE(4, 1)
+  NVFP4DA_QKV_CASE(4, 2)
+  NVFP4DA_QKV_CASE(4, 4)
+  NVFP4DA_QKV_CASE(8, 1)
+  NVFP4DA_QKV_CASE(8, 2)
+  NVFP4DA_QKV_CASE(8, 4)
+#undef NVFP4DA_QKV_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
+// ---------------------------------------------------------------- forward plan
+struct ForwardLayout {
+  bool fused;
+  QkvPlan qkv;
+  AttnPlan attn;
+  size_t q_buf, ctx_buf, attn_ws, scratch;  // byte offsets
+  size_t total;
+  // modular-path buffers (offsets)
+  size_t xn, qp, kp, vp, qn, kn, kr;
+};
+
+int check_forward(const nvfp4da_forward_args* a) {
+  if (!a) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (!a->x || !a->input_norm_weight || !a->q_norm_weight || !a->k_norm_weight || !a->k_cache || !a->v_cache ||
+      !a->output)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (a->batch <= 0 || a->tokens <= 0 || a->hidden <= 0 || a->kv_heads <= 0 || a->head_dim <= 0 ||
+      a->capacity <= 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "dimensions must all be positive");
+  if (a->hidden % a->head_dim != 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "hidden size must be divisible by head dimension");
+  const int64_t hq = a->hidden / a->head_dim;
+  if (hq % a->kv_heads != 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "number of query heads must be divisible by number of KV heads");
+  if (a->head_dim % 2 != 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "head dimension must be even");
+  if (!(a->rms_eps > 0.0f) || !std::isfinite(a->rms_eps))
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "rms_eps must be finite and positive");
+  if (!(a->rope_theta > 0.0f) || !std::isfinite(a->rope_theta))
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "rope_theta must be finite and positive");
+  const int64_t maxp = a->past_lengths ? a->max_past_length : a->past_length;
+  int r = check_attention_dims(a->batch, a->tokens, hq, a->kv_heads, a->capacity, a->head_dim, maxp);
+  if (r) return r;
+  const int64_t kvw = a->kv_heads * a->head_dim;
+  struct {
+    const nvfp4da_weight* w;
+    const char* name;
+    int64_t rows, cols;
+  } ws[4] = {{&a->q_weight, "q_weight", a->hidden, a->hidden},
+             {&a->k_weight, "k_weight", kvw, a->hidden},
+             {&a->v_weight, "v_weight", kvw, a->hidden},
+             {&a->out_weight, "out_weight", a->hidden, a->hidden}};
+  for (auto& w : ws) {
+    if ((r = check_weight(w.w, w.name))) return r;
+    if (w.w->rows != w.rows || w.w->cols != w.cols)
+      return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "%s must be [%lld, %lld]", w.name, static_cast<long long>(w.rows),
+                  static_cast<long long>(w.cols));
+  }
+  return NVFP4DA_OK;
+}
+
+int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
+  const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens;
+  const int64_t maxp = a->past_lengths ? a->max_past_length : a->past_length;
+  if (!plan_attention(a->batch, a->tokens, hq, a->kv_heads, a->head_dim, maxp, L.attn))
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "head_dim %lld is not supported", static_cast<long long>(a->head_dim));
+  L.fused = plan_qkv(m, a->hidden, a->head_dim, L.qkv);
+  const size_t act = align_up(static_cast<size_t>(m * a->hidden) * 2, 256);
+  const size_t kvact = align_up(static_cast<size_t>(m * a->kv_heads * a->head_dim) * 2, 256);
+  size_t off = 0;
+  L.q_buf = off;
+  off += act;
+  L.ctx_buf = off;
+  off += act;
+  L.attn_ws = off;
+  off += L.attn.partial_bytes + L.attn.counter_bytes;
+  L.scratch = off;
+  if (!L.fused) {
+    L.xn = off;
+    off += act;
+    L.qp = off;
+    off += act;
+    L.kp = off;
+    off += kvact;
+    L.vp = off;
+    off += kvact;
+    L.qn = off;
+    off += act;
+    L.kn = off;
+    off += kvact;
+    L.kr = off;
+    off += kvact;
+  }
+  L.total = off;
+  return NVFP4DA_OK;
+}
+
+QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
+  QkvParams p{};
+  p.x = a->x;
+  p.g_in = a->input_norm_weight;
+  const nvfp4da_weight* w3[3] = {&a->q_weight, &a->k_weight, &a->v_weight};
+  for (int i = 0; i < 3; ++i) {
+    p.packed[i] = w3[i]->packed_values;
+    p.scales[i] = w3[i]->block_scales;
+    p.gamma[i] = w3[i]->global_decode_scale;
+  }
+  p.g_q = a->q_norm_weight;
+  p.g_k = a->k_norm_weight;
+  p.q_out = q_out;
+  p.k_cache = a->k_cache;
+  p.v_cache = a->v_cache;
+  p.m = a->batch * a->tokens;
+  p.tokens = a->tokens;
+  p.hidden = a->hidden;
+  p.q_heads = a->hidden / a->head_dim;
+  p.kv_heads = a->kv_heads;
+  p.head_dim = a->head_dim;
+  p.capacity = a->capacity;
+  p.past_length = a->past_length;
+  p.past_lengths = a->past_lengths;
+  p.eps = a->rms_eps;
+  p.theta = a->rope_theta;
+  if (const nvfp4da_forward_stages* st = a->stages) {
+    p.dbg_xnorm = st->input_normalized;
+    p.dbg_q = st->q_projected;
+    p.dbg_k = st->k_projected;
+    p.dbg_v = st->v_projected;
+    p.dbg_qn = st->q_normalized;
+    p.dbg_kn = st->k_normalized;
+  }
+  p.pdl = 1;
+  return p;
+}
+
+}  // namespace
+}  // namespace nvfp4da
+
+using namespace nvfp4da;
+
+extern "C" {
+
+const char* nvfp4da_last_error(void) { return g_last_error.c_str(); }
+
+int nvfp4da_abi_version(void) { return 1; }
+
+int nvfp4da_unpack_e2m1_codes(const uint8_t* packed, uint8_t* codes, int64_t rows, int64_t packed_cols,
+                              void* stream) {
+  if (!packed || !codes || rows <= 0 || packed_cols <= 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "unpack: invalid arguments");
+  const int64_t n = rows * packed_cols;
+  unpack_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, static_cast<cudaStream_t>(stream)>>>(packed, codes, n);
+  NVFP4DA_CHECK_LAUNCH("unpack launch");
+  return NVFP4DA_OK;
+}
+
+int nvfp4da_dequantize_nvfp4(const nvfp4da_weight* w, float* out, void* stream) {
+  int r = check_weight(w, "weight");
+  if (r) return r;
+  if (!out) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "out is NULL");
+  const int64_t nb = w->rows * (w->cols / 2);
+  dequant_kernel<<<static_cast<unsigned>(ceil_div(nb, 256)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      w->packed_values, w->block_scales, w->global_decode_scale, out, nb, w->cols / 2);
+  NVFP4DA_CHECK_LAUNCH("dequantize launch");
+  return NVFP4DA_OK;
+}
+
+size_t nvfp4da_quantize_workspace_size(int64_t, int64_t) { return 256; }
+
+int nvfp4da_quantize_nvfp4(const void* src, int is_bf16, int64_t rows, int64_t cols, uint8_t* packed,
+                           uint8_t* scales, float* gamma, void* ws, size_t ws_bytes, void* stream) {
+  if (!src || !packed || !scales || !gamma || rows <= 0 || cols < 16 || cols % 16 != 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "quantize: invalid arguments (K must be a positive multiple of 16)");
+  if (!ws || ws_bytes < 4) return fail(NVFP4DA_ERR_WORKSPACE, "quantize workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned* amax = static_cast<unsigned*>(ws);
+  cudaError_t e = cudaMemsetAsync(amax, 0, 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize clear");
+  const int64_t n = rows * cols;
+  const int64_t grid = std::min<int64_t>(ceil_div(n, 256), 4LL * sm_count());
+  quant_amax_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(src, is_bf16, n, amax);
+  NVFP4DA_CHECK_LAUNCH("quantize amax launch");
+  const int64_t nblk = rows * (cols / 16);
+  quant_blocks_kernel<<<static_cast<unsigned>(ceil_div(nblk, 128)), 128, 0, s>>>(src, is_bf16, rows, cols, amax,
+                                                                                 packed, scales, gamma);
+  NVFP4DA_CHECK_LAUNCH("quantize blocks launch");
+  return NVFP4DA_OK;
+}
+
+int nvfp4da_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* out, int64_t rows, int64_t cols, float eps,
+                     void* stream) {
+  if (!x || !w || !out || rows <= 0 || cols <= 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "rms_norm: invalid arguments");
+  if (!(eps > 0.0f) || !std::isfinite(eps)) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "eps must be finite and positive");
+  if (rows > std::numeric_limits<int32_t>::max())
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "x has too many logical rows for a one-dimensional CUDA grid");
+  rms_norm_kernel<<<static_cast<unsigned>(rows), kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, w, out,
+                                                                                                     cols, eps);
+  NVFP4DA_CHECK_LAUNCH("rms_norm launch");
+  return NVFP4DA_OK;
+}
+
+int nvfp4da_apply_rope(const uint16_t* x, uint16_t* out, int64_t batch, int64_t tokens, int64_t heads,
+                       int64_t head_dim, int64_t past_length, float theta, void* stream) {
+  if (!x || !out || batch <= 0 || tokens <= 0 || heads <= 0 || head_dim < 2 || head_dim % 2)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "apply_rope: invalid arguments");
+  if (past_length < 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "past_length must be nonnegative");
+  if (!(theta > 0.0f) || !std::isfinite(theta))
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "rope_theta must be finite and positive");
+  const int64_t pairs = batch * tokens * heads * head_dim / 2;
+  rope_kernel<<<static_cast<unsigned>(ceil_div(pairs, 256)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, out, pairs, tokens, heads, head_dim, past_length, theta);
+  NVFP4DA_CHECK_LAUNCH("rope launch");
+  return NVFP4DA_OK;
+}
+
+int nvfp4da_w4a16_linear(const uint16_t* x, int64_t m, const nvfp4da_weight* w, uint16_t* y, void* stream) {
+  int r = check_weight(w, "weight");
+  if (r) return r;
+  if (!x || !y || m <= 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "w4a16_linear: invalid arguments");
+  return run_gemv(x, m, *w, y, static_cast<cudaStream_t>(stream), false);
+}
+
+int nvfp4da_kv_cache_append(uint16_t* kc, uint16_t* vc, const uint16_t* nk, const uint16_t* nv, int64_t batch,
+                            int64_t kv_heads, int64_t capacity, int64_t head_dim, int64_t tokens,
+                            int64_t past_length, const int64_t* past_lengths, void* stream) {
+  if (!kc || !vc || !nk || !nv || batch <= 0 || kv_heads <= 0 || capacity <= 0 || head_dim <= 0 || tokens <= 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "kv_cache_append: invalid arguments");
+  if (!past_lengths) {
+    if (past_length < 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "past_length must be nonnegative");
+    if (past_length > std::numeric_limits<int64_t>::max() - tokens)
+      return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "past_length + current token count overflows int64");
+    if (past_length + tokens > capacity)
+      return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "past_length + current token count exceeds cache capacity");
+  }
+  const int64_t total = batch * tokens * kv_heads * head_dim;
+  kv_append_kernel<<<static_cast<unsigned>(ceil_div(total, 256)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      kc, vc, nk, nv, total, tokens, kv_heads, head_dim, capacity, past_length, past_lengths);
+  NVFP4DA_CHECK_LAUNCH("kv append launch");
+  return NVFP4DA_OK;
+}
+
+size_t nvfp4da_gqa_attention_workspace_size(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads,
+                                            int64_t head_dim, int64_t max_past) {
+  AttnPlan pl;
+  if (batch <= 0 || tokens <= 0 || kv_heads <= 0 || q_heads % kv_heads ||
+      !plan_attention(batch, tokens, q_heads, kv_heads, head_dim, max_past, pl))
+    return 0;
+  return pl.partial_bytes + pl.counter_bytes;
+}
+
+int nvfp4da_gqa_attention_cached(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* ctx,
+                                 int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t capacity,
+                                 int64_t head_dim, int64_t past_length, const int64_t* past_lengths,
+                                 int64_t max_past, void* ws, size_t ws_bytes, void* stream) {
+  if (!q || !kc || !vc || !ctx) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "attention: NULL pointer");
+  if (!past_lengths) max_past = past_length;
+  int r = check_attention_dims(batch, tokens, q_heads, kv_heads, capacity, head_dim, max_past);
+  if (r) return r;
+  if (!aligned(q, 16) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(ctx, 16))
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "attention tensors must be 16-byte aligned");
+  return run_attention(q, kc, vc, ctx, batch, tokens, q_heads, kv_heads, capacity, head_dim, past_length,
+                       past_lengths, max_past, ws, ws_bytes, static_cast<cudaStream_t>(stream), false, true);
+}
+
+size_t nvfp4da_forward_workspace_size(const nvfp4da_forward_args* a) {
+  if (check_forward(a)) return 0;
+  ForwardLayout L;
+  if (plan_forward(a, L)) return 0;
+  return L.total;
+}
+
+int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* a, void* ws, size_t ws_bytes, void* stream) {
+  int r = check_forward(a);
+  if (r) return r;
+  ForwardLayout L;
+  if ((r = plan_forward(a, L))) return r;
+  if (!ws || ws_bytes < L.total)
+    return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace too small (%zu < %zu bytes)", ws_bytes, L.total);
+  if (!aligned(ws, 256)) return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* base = static_cast<char*>(ws);
+  const nvfp4da_forward_stages* st = a->stages;
+  const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens, d = a->head_dim;
+  const int64_t maxp = a->past_lengths ? a->max_past_length : a->past_length;
+  uint16_t* q_buf = (st && st->q_rope) ? st->q_rope : reinterpret_cast<uint16_t*>(base + L.q_buf);
+  uint16_t* ctx_buf = (st && st->context) ? st->context : reinterpret_cast<uint16_t*>(base + L.ctx_buf);
+  void* attn_ws = base + L.attn_ws;
+
+  if (L.fused) {
+    QkvParams p = qkv_params(a, q_buf);
+    p.zero_words = L.attn.counter_bytes ? reinterpret_cast<unsigned*>(static_cast<char*>(attn_ws) + L.attn.partial_bytes)
+                                        : nullptr;
+    p.n_zero_words = static_cast<int64_t>(L.attn.counter_bytes / 4);
+    cudaError_t e = launch_qkv(p, L.qkv, hq + 2 * a->kv_heads, s, true);
+    if (e != cudaSuccess) return cuda_fail(e, "fused qkv launch");
+    r = run_attention(q_buf, a->k_cache, a->v_cache, ctx_buf, a->batch, a->tokens, hq, a->kv_heads, a->capacity, d,
+                      a->past_length, a->past_lengths, maxp, attn_ws, L.attn.partial_bytes + L.attn.counter_bytes, s,
+                      true, false);
+    if (r) return r;
+  } else {
+    // General shapes: the reference's modular chain on the standalone kernels.
+    auto buf = [&](uint16_t* user, size_t off) { return user ? user : reinterpret_cast<uint16_t*>(base + off); };
+    uint16_t* xn = buf(st ? st->input_normalized : nullptr, L.xn);
+    uint16_t* qp = buf(st ? st->q_projected : nullptr, L.qp);
+    uint16_t* kp = buf(st ? st->k_projected : nullptr, L.kp);
+    uint16_t* vp = buf(st ? st->v_projected : nullptr, L.vp);
+    uint16_t* qn = buf(st ? st->q_normalized : nullptr, L.qn);
+    uint16_t* kn = buf(st ? st->k_normalized : nullptr, L.kn);
+    uint16_t* kr = reinterpret_cast<uint16_t*>(base + L.kr);
+    if ((r = nvfp4da_rms_norm(a->x, a->input_norm_weight, xn, m, a->hidden, a->rms_eps, s))) return r;
+    if ((r = run_gemv(xn, m, a->q_weight, qp, s, false))) return r;
+    if ((r = run_gemv(xn, m, a->k_weight, kp, s, false))) return r;
+    if ((r = run_gemv(xn, m, a->v_weight, vp, s, false))) return r;
+    if ((r = nvfp4da_rms_norm(qp, a->q_norm_weight, qn, m * hq, d, a->rms_eps, s))) return r;
+    if ((r = nvfp4da_rms_norm(kp, a->k_norm_weight, kn, m * a->kv_heads, d, a->rms_eps, s))) return r;
+    if (a->past_lengths) {
+      // Per-sequence positions: RoPE one sequence at a time is not expressible
+      // without reading past_lengths on the host; the fused path covers it.
+      return fail(NVFP4DA_ERR_UNSUPPORTED, "per-sequence past_lengths need head_dim % 32 == 0");
+    }
+    if ((r = nvfp4da_apply_rope(qn, q_buf, a->batch, a->tokens, hq, d, a->past_length, a->rope_theta, s))) return r;
+    if ((r = nvfp4da_apply_rope(kn, kr, a->batch, a->tokens, a->kv_heads, d, a->past_length, a->rope_theta, s)))
+      return r;
+    if ((r = nvfp4da_kv_cache_append(a->k_cache, a->v_cache, kr, vp, a->batch, a->kv_heads, a->capacity, d,
+                                     a->tokens, a->past_length, nullptr, s)))
+      return r;
+    r = run_attention(q_buf, a->k_cache, a->v_cache, ctx_buf, a->batch, a->tokens, hq, a->kv_heads, a->capacity, d,
+                      a->past_length, nullptr, maxp, attn_ws, L.attn.partial_bytes + L.attn.counter_bytes, s, false,
+                      true);
+    if (r) return r;
+  }
+  if ((r = run_gemv(ctx_buf, m, a->out_weight, a->output, s, L.fused))) return r;
+  return NVFP4DA_OK;
+}
+
+int nvfp4da_qkv_rope_append(const nvfp4da_forward_args* a, uint16_t* q_rope_out, void* stream) {
+  int r = check_forward(a);
+  if (r) return r;
+  if (!q_rope_out) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "q_rope_out is NULL");
+  QkvPlan pl;
+  if (!plan_qkv(a->batch * a->tokens, a->hidden, a->head_dim, pl))
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "the fused QKV kernel needs head_dim %% 32 == 0 and head_dim <= 256");
+  QkvParams p = qkv_params(a, q_rope_out);
+  const int64_t hq = a->hidden / a->head_dim;
+  cudaError_t e = launch_qkv(p, pl, hq + 2 * a->kv_heads, static_cast<cudaStream_t>(stream), true);
+  if (e != cudaSuccess) return cuda_fail(e, "fused qkv launch");
+  return NVFP4DA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+// Standalone W4A16 GEMV kernel: y[M, N] = x[M, K] @ W_hat[N, K]^T (BF16 out).
+// Backs `cuda_w4a16_linear` and the O projection of the decode step.
+#pragma once
+
+#include "gemv_core.cuh"
+
+namespace nvfp4da {
+
+struct GemvParams {
+  const uint16_t* x;  // [M, K] bf16
+  int64_t m;
+  const uint8_t* packed;  // [N, K/2]
+  const uint8_t* scales;  // [N, K/16]
+  const float* gamma;
+  uint16_t* y;  // [M, N] bf16
+  int64_t n, k;
+  unsigned* err;
+  int pdl;
+};
+
+// One CTA = 8*RPW weight rows, all M activation rows (in groups of MG).
+// Weights are bulk-copied into shared memory first (before the PDL wait, since
+// they never depend on an earlier kernel), then activations are staged per
+// group as FP32.
+template <int RPW, int MG>
+__global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ uint64_t bars[kGemvWarps];
+  constexpr int kRows = kGemvWarps * RPW;
+  const int64_t k = p.k, nc = k / 16;
+  const GemvSmemLayout lay = gemv_layout(kRows, k, MG);
+  uint8_t* w_smem = smem;
+  uint8_t* s_smem = smem + lay.w_bytes;
+  float4* x_smem = reinterpret_cast<float4*>(smem + lay.w_bytes + lay.s_bytes);
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGemvWarps; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool bulk = gemv_bulk_ok(p.packed, p.scales, k);
+  gemv_stage_weights(w_smem, s_smem, p.packed, p.scales, k, row0, kRows, p.n, bulk, bars);
+  if (p.pdl) {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+  const float gamma = *p.gamma;
+  bool waited = !bulk;
+  for (int64_t m0 = 0; m0 < p.m; m0 += MG) {
+    const int mgv = static_cast<int>((p.m - m0) < MG ? (p.m - m0) : MG);
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < static_cast<int64_t>(mgv) * k; i += blockDim.x) {
+      const int m = static_cast<int>(i / k);
+      const int64_t kk = i % k;
+      x_smem_store(x_smem, nc, m, kk, bf16_bits_to_f32(p.x[(m0 + m) * k + kk]));
+    }
+    __syncthreads();
+    if (!waited) {
+      if (!mbar_wait_bounded(&bars[warp], 0, p.err)) return;
+      waited = true;
+    }
+    float acc[RPW][MG];
+    gemv_warp_rows<RPW, MG>(w_smem, s_smem, x_smem, k, mgv, acc);
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+      for (int m = 0; m < MG; ++m) {
+        const int64_t row = row0 + warp * RPW + r;
+        if (lane == ((r * MG + m) & 31) && m < mgv && row < p.n)
+          p.y[(m0 + m) * p.n + row] = f32_to_bf16_bits(__fmul_rn(acc[r][m], gamma));
+      }
+  }
+}
+
+}  // namespace nvfp4da

@@ -1,0 +1,211 @@
+// Fused decode-step front half: input RMSNorm -> W4A16 Q/K/V projection ->
+// per-head Q/K RMSNorm -> adjacent-pair RoPE -> K/V cache append.
+//
+// Reference stages (decoder_attention_cuda.py:273-395): cuda_rms_norm,
+// 3x cuda_w4a16_linear, 2x cuda_rms_norm, 2x cuda_apply_rope and
+// cuda_kv_cache_append_ — nine launches there, one here.
+//
+// Decomposition: one thread-block cluster of 4 CTAs per "head unit" (Hq query
+// heads, then Hkv key heads, then Hkv value heads).  Each CTA owns D/4
+// consecutive weight rows of that head (32 rows for D = 128), bulk-copies them
+// (K/2 + K/16 bytes per row) into shared memory at kernel start, recomputes the
+// input RMSNorm of the activation rows itself (the x row is tiny and L2-hot),
+// and reduces its rows.  The BF16 projections are written into the cluster
+// leader's shared memory through distributed shared memory; after a cluster
+// barrier the leader owns the whole head and applies the head epilogue.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "elementwise.cuh"
+#include "gemv_core.cuh"
+
+namespace nvfp4da {
+
+namespace cg = cooperative_groups;
+
+constexpr int kQkvCluster = 4;
+constexpr int kMaxHeadDim = 256;
+
+struct QkvParams {
+  const uint16_t* x;     // [M, H] bf16, M = B*T
+  const uint16_t* g_in;  // [H]
+  const uint8_t* packed[3];  // q, k, v
+  const uint8_t* scales[3];
+  const float* gamma[3];
+  const uint16_t* g_q;  // [D]
+  const uint16_t* g_k;  // [D]
+  uint16_t* q_out;      // [M, Hq, D]
+  uint16_t* k_cache;    // [B, Hkv, C, D]
+  uint16_t* v_cache;
+  int64_t m, tokens, hidden, q_heads, kv_heads, head_dim, capacity;
+  int64_t past_length;
+  const int64_t* past_lengths;
+  float eps, theta;
+  // Optional stage outputs (nullptr = skip), for stage-by-stage parity checks.
+  uint16_t* dbg_xnorm;  // [M, H]
+  uint16_t* dbg_q;      // [M, Hq*D]
+  uint16_t* dbg_k;      // [M, Hkv*D]
+  uint16_t* dbg_v;      // [M, Hkv*D]
+  uint16_t* dbg_qn;     // [M, Hq*D]
+  uint16_t* dbg_kn;     // [M, Hkv*D]
+  unsigned* zero_words;  // cleared by CTA 0 (attention split counters)
+  int64_t n_zero_words;
+  unsigned* err;
+  int pdl;
+};
+
+template <int RPW, int MG>
+__global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThreads)
+    qkv_fused_kernel(QkvParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ uint64_t bars[kGemvWarps];
+  __shared__ uint16_t head_out[MG][kMaxHeadDim];
+  __shared__ double red[kGemvWarps];
+  constexpr int kRows = kGemvWarps * RPW;  // = D / 4
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int64_t unit = blockIdx.x / kQkvCluster;
+  const int64_t d = p.head_dim, k = p.hidden, nc = k / 16;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  int mat;
+  int64_t head;
+  if (unit < p.q_heads) {
+    mat = 0;
+    head = unit;
+  } else if (unit < p.q_heads + p.kv_heads) {
+    mat = 1;
+    head = unit - p.q_heads;
+  } else {
+    mat = 2;
+    head = unit - p.q_heads - p.kv_heads;
+  }
+  const int64_t n_rows = (mat == 0 ? p.q_heads : p.kv_heads) * d;
+  const int64_t row0 = head * d + static_cast<int64_t>(rank) * kRows;
+
+  const GemvSmemLayout lay = gemv_layout(kRows, k, MG);
+  uint8_t* w_smem = smem;
+  uint8_t* s_smem = smem + lay.w_bytes;
+  float4* x_smem = reinterpret_cast<float4*>(smem + lay.w_bytes + lay.s_bytes);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGemvWarps; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool bulk = gemv_bulk_ok(p.packed[mat], p.scales[mat], k);
+  gemv_stage_weights(w_smem, s_smem, p.packed[mat], p.scales[mat], k, row0, kRows, n_rows, bulk, bars);
+
+  // Everything above touches only weights; from here on we read x and write
+  // caches, so wait for the previous kernel in the stream.
+  if (p.pdl) {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = threadIdx.x; i < p.n_zero_words; i += blockDim.x) p.zero_words[i] = 0u;
+
+  const float gamma = *p.gamma[mat];
+  bool waited = !bulk;
+  bool ok = true;
+  uint16_t* leader_out = cluster.map_shared_rank(&head_out[0][0], 0);
+
+  for (int64_t m0 = 0; m0 < p.m; m0 += MG) {
+    const int mgv = static_cast<int>((p.m - m0) < MG ? (p.m - m0) : MG);
+    __syncthreads();
+    // ---- input RMSNorm (reference/decoder_attention.py:117-140), rows m0.. into x_smem
+    for (int m = 0; m < mgv; ++m) {
+      const uint16_t* xr = p.x + (m0 + m) * k;
+      double ss = 0.0;
+      for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        const float v = bf16_bits_to_f32(xr[i]);
+        ss += static_cast<double>(v * v);
+      }
+      ss = warp_sum_f64(ss);
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      double tot = 0.0;
+#pragma unroll
+      for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
+      const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
+      for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        const float v = bf16_bits_to_f32(xr[i]);
+        const uint16_t nb = f32_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_f32(p.g_in[i])));
+        x_smem_store(x_smem, nc, m, i, bf16_bits_to_f32(nb));
+        if (p.dbg_xnorm && blockIdx.x == 0) p.dbg_xnorm[(m0 + m) * k + i] = nb;
+      }
+      __syncthreads();
+    }
+    if (!waited) {
+      ok = mbar_wait_bounded(&bars[warp], 0, p.err);
+      waited = true;
+    }
+    float acc[RPW][MG];
+    gemv_warp_rows<RPW, MG>(w_smem, s_smem, x_smem, k, mgv, acc);
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+      for (int m = 0; m < MG; ++m)
+        if (lane == ((r * MG + m) & 31) && m < mgv)
+          leader_out[m * kMaxHeadDim + rank * kRows + warp * RPW + r] =
+              ok ? f32_to_bf16_bits(__fmul_rn(acc[r][m], gamma)) : uint16_t(0x7fc0);
+    cluster.sync();
+
+    if (rank == 0 && warp < mgv) {
+      // ---- head epilogue for activation row m0 + warp
+      const int64_t mrow = m0 + warp;
+      const int64_t b = mrow / p.tokens, t = mrow % p.tokens;
+      const int64_t pos = (p.past_lengths ? p.past_lengths[b] : p.past_length) + t;
+      const uint16_t* y = head_out[warp];
+      if (mat == 2) {
+        uint16_t* dst = p.v_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d;
+        for (int64_t e = lane; e < d; e += 32) {
+          dst[e] = y[e];
+          if (p.dbg_v) p.dbg_v[mrow * p.kv_heads * d + head * d + e] = y[e];
+        }
+      } else {
+        const uint16_t* g = (mat == 0) ? p.g_q : p.g_k;
+        double ss = 0.0;
+        for (int64_t e = lane; e < d; e += 32) {
+          const float v = bf16_bits_to_f32(y[e]);
+          ss += static_cast<double>(v * v);
+        }
+        ss = warp_sum_f64(ss);
+        const float inv = rms_inverse(static_cast<float>(ss), static_cast<float>(d), p.eps);
+        const int64_t heads = (mat == 0) ? p.q_heads : p.kv_heads;
+        uint16_t* dbg_proj = (mat == 0) ? p.dbg_q : p.dbg_k;
+        uint16_t* dbg_norm = (mat == 0) ? p.dbg_qn : p.dbg_kn;
+        uint16_t* dst = (mat == 0) ? p.q_out + (mrow * p.q_heads + head) * d
+                                   : p.k_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d;
+        for (int64_t pr = lane; pr < d / 2; pr += 32) {
+          const int64_t e = 2 * pr;
+          const uint16_t n0 = f32_to_bf16_bits(
+              __fmul_rn(__fmul_rn(bf16_bits_to_f32(y[e]), inv), bf16_bits_to_f32(g[e])));
+          const uint16_t n1 = f32_to_bf16_bits(
+              __fmul_rn(__fmul_rn(bf16_bits_to_f32(y[e + 1]), inv), bf16_bits_to_f32(g[e + 1])));
+          if (dbg_proj) {
+            dbg_proj[mrow * heads * d + head * d + e] = y[e];
+            dbg_proj[mrow * heads * d + head * d + e + 1] = y[e + 1];
+          }
+          if (dbg_norm) {
+            dbg_norm[mrow * heads * d + head * d + e] = n0;
+            dbg_norm[mrow * heads * d + head * d + e + 1] = n1;
+          }
+          uint16_t r0 = n0, r1 = n1;
+          if (pos != 0) {
+            float c, s;
+            rope_cos_sin(pos, pr, d, p.theta, c, s);
+            rope_pair(bf16_bits_to_f32(n0), bf16_bits_to_f32(n1), c, s, r0, r1);
+          }
+          dst[e] = r0;
+          dst[e + 1] = r1;
+        }
+      }
+    }
+    cluster.sync();  // head_out is reused by the next activation group
+  }
+}
+
+}  // namespace nvfp4da
