@@ -116,7 +116,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     pdl_wait();
   }
 
-  const int64_t visible = seq_past(p, b) + t + 1;  // keys 0 .. P_b + t
+  int64_t visible = seq_past(p, b) + t + 1;  // keys 0 .. P_b + t
+  // Never read beyond the physical capacity, whatever a device-side length says.
+  if (visible > p.capacity) visible = p.capacity;
   const int64_t s0 = static_cast<int64_t>(split) * p.split_len;
   int64_t s1 = s0 + p.split_len;
   if (s1 > visible) s1 = visible;

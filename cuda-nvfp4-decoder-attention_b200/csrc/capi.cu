@@ -8,7 +8,10 @@
 #include <cstdio>
 #include <cstring>
 #include <limits>
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/nvfp4_decoder_attention.h"
 #include "attention.cuh"
@@ -32,6 +35,7 @@ int fail(int code, const char* fmt, ...) {
 }
 
 int cuda_fail(cudaError_t e, const char* what) {
+  cudaGetLastError();  // clear a non-sticky launch error so later calls start clean
   return fail(NVFP4DA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
@@ -60,16 +64,22 @@ int sm_count() {
   return n;
 }
 
-// Raise the dynamic shared-memory limit of `fn` on the current device once.
+// Raise the dynamic shared-memory limit of `fn` on the current device once
+// (cached per kernel and device; all instantiations of one kernel template
+// share a function type, so the key is the function address).
+std::mutex g_smem_mutex;
+std::map<std::pair<const void*, int>, uint32_t> g_smem_set;
+
 template <typename F>
 cudaError_t ensure_smem(F* fn, uint32_t bytes) {
-  static uint32_t set_bytes[kMaxDevices] = {0};
-  const int dev = current_device();
   if (bytes <= 48 * 1024) return cudaSuccess;
-  if (dev < kMaxDevices && set_bytes[dev] >= bytes) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e == cudaSuccess && dev < kMaxDevices) set_bytes[dev] = bytes;
+  const void* key = reinterpret_cast<const void*>(fn);
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_smem_mutex);
+  auto it = g_smem_set.find({key, dev});
+  if (it != g_smem_set.end() && it->second >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(key, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) g_smem_set[{key, dev}] = bytes;
   return e;
 }
 

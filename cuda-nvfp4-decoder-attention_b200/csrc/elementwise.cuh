@@ -101,6 +101,7 @@ __global__ void kv_append_kernel(uint16_t* kc, uint16_t* vc, const uint16_t* nk,
   const int64_t t = r % tokens;
   const int64_t b = r / tokens;
   const int64_t p = past_lengths ? past_lengths[b] : past_length;
+  if (p < 0 || p + t >= capacity) return;  // slot outside the cache: not written
   const int64_t dst = ((b * kv_heads + h) * capacity + p + t) * head_dim + d;
   kc[dst] = nk[i];
   vc[dst] = nv[i];

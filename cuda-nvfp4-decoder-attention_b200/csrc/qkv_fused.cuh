@@ -158,11 +158,15 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
       const int64_t mrow = m0 + warp;
       const int64_t b = mrow / p.tokens, t = mrow % p.tokens;
       const int64_t pos = (p.past_lengths ? p.past_lengths[b] : p.past_length) + t;
+      // A per-sequence length read from device memory cannot be checked on the
+      // host: a slot outside [0, C) is not written (the caller's contract is
+      // 0 <= P_b and P_b + T <= C).
+      const bool slot_ok = pos >= 0 && pos < p.capacity;
       const uint16_t* y = head_out[warp];
       if (mat == 2) {
-        uint16_t* dst = p.v_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d;
+        uint16_t* dst = slot_ok ? p.v_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d : nullptr;
         for (int64_t e = lane; e < d; e += 32) {
-          dst[e] = y[e];
+          if (dst) dst[e] = y[e];
           if (p.dbg_v) p.dbg_v[mrow * p.kv_heads * d + head * d + e] = y[e];
         }
       } else {
@@ -178,7 +182,8 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
         uint16_t* dbg_proj = (mat == 0) ? p.dbg_q : p.dbg_k;
         uint16_t* dbg_norm = (mat == 0) ? p.dbg_qn : p.dbg_kn;
         uint16_t* dst = (mat == 0) ? p.q_out + (mrow * p.q_heads + head) * d
-                                   : p.k_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d;
+                        : slot_ok  ? p.k_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d
+                                   : nullptr;
         for (int64_t pr = lane; pr < d / 2; pr += 32) {
           const int64_t e = 2 * pr;
           const uint16_t n0 = f32_to_bf16_bits(
@@ -199,8 +204,10 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
             rope_cos_sin(pos, pr, d, p.theta, c, s);
             rope_pair(bf16_bits_to_f32(n0), bf16_bits_to_f32(n1), c, s, r0, r1);
           }
-          dst[e] = r0;
-          dst[e + 1] = r1;
+          if (dst) {
+            dst[e] = r0;
+            dst[e + 1] = r1;
+          }
         }
       }
     }

@@ -51,7 +51,8 @@ def test_every_byte_and_every_scale_code_decodes_exactly(capi):
     deq = capi.dequantize(dev_weight(s)).cpu().numpy()
     ref = oracle.dequantize(s)
     assert np.array_equal(deq.view(np.uint32), ref.view(np.uint32))
-    assert np.signbit(deq[0, 1]) and deq[0, 1] == 0.0  # byte 0x80 high nibble: code 0x8 is -0.0
+    # byte 0x80 (column 0x80) holds code 0x8 in its high nibble: -0.0
+    assert np.signbit(deq[0, 2 * 0x80 + 1]) and deq[0, 2 * 0x80 + 1] == 0.0
 
 
 @pytest.mark.parametrize("case", QUANT_CASES)
