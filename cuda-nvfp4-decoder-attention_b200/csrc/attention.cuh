@@ -111,25 +111,43 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   const int64_t group = p.q_heads / p.kv_heads;
   const int64_t h0 = static_cast<int64_t>(kvh) * group + static_cast<int64_t>(hg) * GH;
 
-  if (p.pdl) {
-    pdl_launch_dependents();
-    pdl_wait();
-  }
-
-  int64_t visible = seq_past(p, b) + t + 1;  // keys 0 .. P_b + t
-  // Never read beyond the physical capacity, whatever a device-side length says.
+  // Keys 0 .. P_b + t; never read beyond the physical capacity, whatever a
+  // device-side length says.
+  const int64_t pb = seq_past(p, b);
+  int64_t visible = pb + t + 1;
   if (visible > p.capacity) visible = p.capacity;
   const int64_t s0 = static_cast<int64_t>(split) * p.split_len;
   int64_t s1 = s0 + p.split_len;
   if (s1 > visible) s1 = visible;
 
+  const uint16_t* kbase = p.k_cache + (b * p.kv_heads + kvh) * p.capacity * d;
+  const uint16_t* vbase = p.v_cache + (b * p.kv_heads + kvh) * p.capacity * d;
+
+  // Before waiting on the kernel that produced q (the fused QKV kernel, which
+  // writes only slots >= P_b), prefetch this warp's first chunk of cache rows
+  // below P_b.  Rows at or above P_b are loaded after the wait.
+  float kr[NPOS][EPL], vr[NPOS][EPL];
+  int64_t c0 = s0 + static_cast<int64_t>(warp) * NPOS;
+#pragma unroll
+  for (int j = 0; j < NPOS; ++j) {
+    const int64_t pos = c0 + j;
+    if (pos < s1 && pos < pb) {
+      load_row<EPL>(kbase + pos * d, lane, d, kr[j]);
+      load_row<EPL>(vbase + pos * d, lane, d, vr[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) kr[j][e] = vr[j][e] = 0.0f;
+    }
+  }
+  if (p.pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+
   // q for GH heads, this lane's slice.
   float q[GH][EPL];
 #pragma unroll
   for (int g = 0; g < GH; ++g) load_row<EPL>(p.q + ((bt * p.q_heads) + h0 + g) * d, lane, d, q[g]);
-
-  const uint16_t* kbase = p.k_cache + (b * p.kv_heads + kvh) * p.capacity * d;
-  const uint16_t* vbase = p.v_cache + (b * p.kv_heads + kvh) * p.capacity * d;
 
   float m_run[GH], l_run[GH], acc[GH][EPL];
 #pragma unroll
@@ -140,15 +158,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     for (int e = 0; e < EPL; ++e) acc[g][e] = 0.0f;
   }
 
-  for (int64_t c0 = s0 + static_cast<int64_t>(warp) * NPOS; c0 < s1; c0 += kAttnWarps * NPOS) {
-    float kr[NPOS][EPL], vr[NPOS][EPL];
+  for (bool first = true; c0 < s1; c0 += kAttnWarps * NPOS, first = false) {
 #pragma unroll
     for (int j = 0; j < NPOS; ++j) {
       const int64_t pos = c0 + j;
-      if (pos < s1) {
+      const bool need = pos < s1 && (!first || pos >= pb);
+      if (need) {
         load_row<EPL>(kbase + pos * d, lane, d, kr[j]);
         load_row<EPL>(vbase + pos * d, lane, d, vr[j]);
-      } else {
+      } else if (!first) {
 #pragma unroll
         for (int e = 0; e < EPL; ++e) kr[j][e] = vr[j][e] = 0.0f;
       }
@@ -251,8 +269,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   }
   if (single) return;
 
-  // ---- last CTA of this (b, t, head group) combines all splits
+  // ---- last CTA of this (b, t, head group) combines all splits.
   __shared__ unsigned s_last;
+  __shared__ float head_l[GH];
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -264,22 +283,43 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // Stage every split's (m, l) for the GH heads in shared memory (sm_o is free
+  // now; the host caps splits at 64 * EPL so 2 * GH * splits floats fit), then
+  // turn m into the rescale weights exp(m_s - M).
+  const int ns = p.splits;
+  float* sw = &sm_o[0][0][0];
+  float* sl = sw + GH * ns;
+  for (int i = threadIdx.x; i < GH * ns; i += kAttnThreads) {
+    const int g = i / ns, sp = i % ns;
+    const float* src = part_base + ((bt * p.q_heads + h0 + g) * ns + sp) * (d + 2);
+    sw[i] = __ldcg(src + d);
+    sl[i] = __ldcg(src + d + 1);
+  }
+  __syncthreads();
+  for (int g = warp; g < GH; g += kAttnWarps) {
+    float mx = -INFINITY;
+    for (int sp = lane; sp < ns; sp += 32) mx = fmaxf(mx, sw[g * ns + sp]);
+    mx = warp_max_f32(mx);
+    float l = 0.0f;
+    for (int sp = lane; sp < ns; sp += 32) {
+      const float ms = sw[g * ns + sp];
+      const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
+      sw[g * ns + sp] = f;
+      l = fmaf(sl[g * ns + sp], f, l);
+    }
+    l = warp_sum_f32(l);
+    if (lane == 0) head_l[g] = l;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < GH * d; idx += kAttnThreads) {
     const int g = static_cast<int>(idx / d);
     const int64_t e = idx % d;
     const int64_t row = bt * p.q_heads + h0 + g;
-    const float* src = part_base + row * p.splits * (d + 2);
-    float mx = -INFINITY;
-    for (int s = 0; s < p.splits; ++s) mx = fmaxf(mx, __ldcg(src + s * (d + 2) + d));
-    float l = 0.0f, o = 0.0f;
-    for (int s = 0; s < p.splits; ++s) {
-      const float ms = __ldcg(src + s * (d + 2) + d);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - mx);
-      l = fmaf(__ldcg(src + s * (d + 2) + d + 1), f, l);
-      o = fmaf(__ldcg(src + s * (d + 2) + e), f, o);
-    }
-    p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
+    const float* src = part_base + row * ns * (d + 2) + e;
+    float o = 0.0f;
+#pragma unroll 8
+    for (int sp = 0; sp < ns; ++sp) o = fmaf(__ldcg(src + sp * (d + 2)), sw[g * ns + sp], o);
+    p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, head_l[g]));
   }
 }
 

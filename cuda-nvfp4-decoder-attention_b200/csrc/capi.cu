@@ -211,8 +211,11 @@ bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_h
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, ceil_div(visible, chunk)));
   int64_t split_len = ceil_div(ceil_div(visible, splits), chunk) * chunk;
   splits = ceil_div(visible, split_len);
-  if (splits > 65535) {
-    splits = 65535;
+  // The last-CTA combine stages 2 * GH * splits floats in the CTA's
+  // 4 * GH * 32 * EPL-float output buffer: at most 64 * EPL splits.
+  const int64_t max_splits = 64LL * epl;
+  if (splits > max_splits) {
+    splits = max_splits;
     split_len = ceil_div(ceil_div(visible, splits), chunk) * chunk;
     splits = ceil_div(visible, split_len);
   }
@@ -325,8 +328,8 @@ bool plan_qkv(int64_t m, int64_t hidden, int64_t head_dim, QkvPlan& pl) {
   if (rpw != 1 && rpw != 2 && rpw != 4 && rpw != 8) return false;
   int mg = m <= 1 ? 1 : (m == 2 ? 2 : 4);
   for (;;) {
-    const uint32_t bytes = gemv_layout(kGemvWarps * rpw, hidden, mg).total();
-    if (bytes <= kMaxDynSmem - 8 * 1024) {
+    const uint32_t bytes = qkv_layout(kGemvWarps * rpw, hidden, head_dim, mg).total();
+    if (bytes <= kMaxDynSmem - 12 * 1024) {
       pl = {rpw, mg, bytes};
       return true;
     }

@@ -164,4 +164,39 @@ __device__ __forceinline__ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// Copy `bytes` from global to this CTA's shared memory.  If both ends are
+// 16-byte aligned and the size is a multiple of 16, thread 0 issues one bulk
+// async copy on `bar` and every thread waits on `parity`; otherwise all threads
+// copy with plain loads.  Must be called by every thread of the CTA; ends with
+// the data visible to the whole CTA.  Returns false if the bounded wait gave up.
+__device__ __forceinline__ bool stage_to_smem(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint32_t parity, unsigned* err) {
+  if (bytes == 0) return true;
+  const bool bulk = aligned16(dst) && aligned16(src) && (bytes % 16 == 0);
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar, bytes);
+      bulk_g2s(dst, src, bytes, bar);
+    }
+    return mbar_wait_bounded(bar, parity, err);
+  }
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  const uint8_t* s = static_cast<const uint8_t*>(src);
+  for (uint32_t i = threadIdx.x; i < bytes; i += blockDim.x) d[i] = s[i];
+  __syncthreads();
+  return true;
+}
+
+// Issue (thread 0) a bulk copy whose completion is awaited later with
+// mbar_wait_bounded(bar, parity); returns false (nothing issued) when the
+// addresses or size do not allow a bulk copy.
+__device__ __forceinline__ bool bulk_prefetch(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  if (!(aligned16(dst) && aligned16(src) && (bytes % 16 == 0))) return false;
+  if (threadIdx.x == 0 && bytes) {
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_g2s(dst, src, bytes, bar);
+  }
+  return true;
+}
+
 }  // namespace nvfp4da

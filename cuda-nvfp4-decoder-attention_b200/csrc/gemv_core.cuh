@@ -23,10 +23,15 @@ constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * kWarp;
 
 struct GemvSmemLayout {
-  uint32_t w_bytes;  // rows * K/2, rounded up to 16
-  uint32_t s_bytes;  // rows * K/16, rounded up to 16
-  uint32_t x_bytes;  // MG * K * 4
-  uint32_t total() const { return w_bytes + s_bytes + x_bytes; }
+  uint32_t w_bytes;   // rows * K/2, rounded up to 16
+  uint32_t s_bytes;   // rows * K/16, rounded up to 16
+  uint32_t x_bytes;   // MG * K * 4   (FP32, quad-interleaved)
+  uint32_t xs_bytes;  // MG * K * 2   (BF16 staging of the raw activation rows)
+  __host__ __device__ uint32_t w_off() const { return 0; }
+  __host__ __device__ uint32_t s_off() const { return w_bytes; }
+  __host__ __device__ uint32_t x_off() const { return w_bytes + s_bytes; }
+  __host__ __device__ uint32_t xs_off() const { return w_bytes + s_bytes + x_bytes; }
+  __host__ __device__ uint32_t total() const { return w_bytes + s_bytes + x_bytes + xs_bytes; }
 };
 
 __host__ __device__ inline uint32_t round16(uint64_t v) { return static_cast<uint32_t>((v + 15) & ~uint64_t(15)); }
@@ -36,6 +41,7 @@ __host__ __device__ inline GemvSmemLayout gemv_layout(int rows, int64_t k, int m
   l.w_bytes = round16(static_cast<uint64_t>(rows) * (k / 2));
   l.s_bytes = round16(static_cast<uint64_t>(rows) * (k / 16));
   l.x_bytes = static_cast<uint32_t>(static_cast<uint64_t>(mg) * k * 4);
+  l.xs_bytes = round16(static_cast<uint64_t>(mg) * k * 2);
   return l;
 }
 

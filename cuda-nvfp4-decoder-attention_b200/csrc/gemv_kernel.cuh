@@ -26,36 +26,41 @@ template <int RPW, int MG>
 __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ uint64_t bars[kGemvWarps];
+  __shared__ uint64_t xbar;
   constexpr int kRows = kGemvWarps * RPW;
   const int64_t k = p.k, nc = k / 16;
   const GemvSmemLayout lay = gemv_layout(kRows, k, MG);
-  uint8_t* w_smem = smem;
-  uint8_t* s_smem = smem + lay.w_bytes;
-  float4* x_smem = reinterpret_cast<float4*>(smem + lay.w_bytes + lay.s_bytes);
+  uint8_t* w_smem = smem + lay.w_off();
+  uint8_t* s_smem = smem + lay.s_off();
+  float4* x_smem = reinterpret_cast<float4*>(smem + lay.x_off());
+  uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + lay.xs_off());
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemvWarps; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
+  // Weights never depend on an earlier kernel: start streaming them before
+  // the programmatic-dependency wait.
   const bool bulk = gemv_bulk_ok(p.packed, p.scales, k);
   gemv_stage_weights(w_smem, s_smem, p.packed, p.scales, k, row0, kRows, p.n, bulk, bars);
-  if (p.pdl) {
-    pdl_launch_dependents();
-    pdl_wait();
-  }
   const float gamma = *p.gamma;
+  if (p.pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
   bool waited = !bulk;
-  for (int64_t m0 = 0; m0 < p.m; m0 += MG) {
+  int group = 0;
+  for (int64_t m0 = 0; m0 < p.m; m0 += MG, ++group) {
     const int mgv = static_cast<int>((p.m - m0) < MG ? (p.m - m0) : MG);
-    __syncthreads();
-    for (int64_t i = threadIdx.x; i < static_cast<int64_t>(mgv) * k; i += blockDim.x) {
-      const int m = static_cast<int>(i / k);
-      const int64_t kk = i % k;
-      x_smem_store(x_smem, nc, m, kk, bf16_bits_to_f32(p.x[(m0 + m) * k + kk]));
-    }
+    __syncthreads();  // staging buffers are free again
+    if (!stage_to_smem(x_stage, p.x + m0 * k, static_cast<uint32_t>(mgv * k * 2), &xbar, group & 1, p.err))
+      return;
+    for (int64_t i = threadIdx.x; i < static_cast<int64_t>(mgv) * k; i += blockDim.x)
+      x_smem_store(x_smem, nc, static_cast<int>(i / k), i % k, bf16_bits_to_f32(x_stage[i]));
     __syncthreads();
     if (!waited) {
       if (!mbar_wait_bounded(&bars[warp], 0, p.err)) return;

@@ -55,12 +55,33 @@ struct QkvParams {
   int pdl;
 };
 
+// Dynamic shared memory of the fused kernel: the GEMV layout followed by the
+// input-norm gain [K] and the two head-norm gains [D] (BF16).
+struct QkvSmemLayout {
+  GemvSmemLayout g;
+  uint32_t gin_bytes, gh_bytes;
+  __host__ __device__ uint32_t gin_off() const { return g.total(); }
+  __host__ __device__ uint32_t gq_off() const { return g.total() + gin_bytes; }
+  __host__ __device__ uint32_t gk_off() const { return g.total() + gin_bytes + gh_bytes; }
+  __host__ __device__ uint32_t total() const { return g.total() + gin_bytes + 2 * gh_bytes; }
+};
+
+__host__ __device__ inline QkvSmemLayout qkv_layout(int rows, int64_t k, int64_t d, int mg) {
+  QkvSmemLayout l;
+  l.g = gemv_layout(rows, k, mg);
+  l.gin_bytes = round16(static_cast<uint64_t>(k) * 2);
+  l.gh_bytes = round16(static_cast<uint64_t>(d) * 2);
+  return l;
+}
+
 template <int RPW, int MG>
 __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThreads)
     qkv_fused_kernel(QkvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ uint64_t bars[kGemvWarps];
+  __shared__ uint64_t xbar, gbar;
   __shared__ uint16_t head_out[MG][kMaxHeadDim];
+  __shared__ float2 rope_cs[MG][kMaxHeadDim / 2];
   __shared__ double red[kGemvWarps];
   constexpr int kRows = kGemvWarps * RPW;  // = D / 4
 
@@ -84,40 +105,84 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
   }
   const int64_t n_rows = (mat == 0 ? p.q_heads : p.kv_heads) * d;
   const int64_t row0 = head * d + static_cast<int64_t>(rank) * kRows;
+  const bool leader = (rank == 0);
 
-  const GemvSmemLayout lay = gemv_layout(kRows, k, MG);
-  uint8_t* w_smem = smem;
-  uint8_t* s_smem = smem + lay.w_bytes;
-  float4* x_smem = reinterpret_cast<float4*>(smem + lay.w_bytes + lay.s_bytes);
+  const QkvSmemLayout lay = qkv_layout(kRows, k, d, MG);
+  uint8_t* w_smem = smem + lay.g.w_off();
+  uint8_t* s_smem = smem + lay.g.s_off();
+  float4* x_smem = reinterpret_cast<float4*>(smem + lay.g.x_off());
+  uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + lay.g.xs_off());
+  uint16_t* gin_s = reinterpret_cast<uint16_t*>(smem + lay.gin_off());
+  uint16_t* gq_s = reinterpret_cast<uint16_t*>(smem + lay.gq_off());
+  uint16_t* gk_s = reinterpret_cast<uint16_t*>(smem + lay.gk_off());
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemvWarps; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&xbar, 1);
+    mbar_init(&gbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
+
+  // ---- Before the programmatic-dependency wait: everything that no earlier
+  // kernel writes (weights, gains, gamma, and the RoPE table when the
+  // positions are a host scalar).
   const bool bulk = gemv_bulk_ok(p.packed[mat], p.scales[mat], k);
   gemv_stage_weights(w_smem, s_smem, p.packed[mat], p.scales[mat], k, row0, kRows, n_rows, bulk, bars);
+  const bool gains_bulk = aligned16(p.g_in) && aligned16(p.g_q) && aligned16(p.g_k) && (k * 2) % 16 == 0 &&
+                          (d * 2) % 16 == 0;
+  if (gains_bulk && threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&gbar, static_cast<uint32_t>(k * 2 + 2 * d * 2));
+    bulk_g2s(gin_s, p.g_in, static_cast<uint32_t>(k * 2), &gbar);
+    bulk_g2s(gq_s, p.g_q, static_cast<uint32_t>(d * 2), &gbar);
+    bulk_g2s(gk_s, p.g_k, static_cast<uint32_t>(d * 2), &gbar);
+  }
+  const float gamma = *p.gamma[mat];
+  const bool table_early = leader && mat < 2 && p.past_lengths == nullptr;
+  auto fill_rope_table = [&](int64_t m0, int mgv) {
+    for (int64_t i = threadIdx.x; i < static_cast<int64_t>(mgv) * (d / 2); i += blockDim.x) {
+      const int m = static_cast<int>(i / (d / 2));
+      const int64_t pr = i % (d / 2);
+      const int64_t mrow = m0 + m;
+      const int64_t b = mrow / p.tokens, t = mrow % p.tokens;
+      const int64_t pos = (p.past_lengths ? p.past_lengths[b] : p.past_length) + t;
+      float c = 1.0f, sn = 0.0f;
+      if (pos != 0) rope_cos_sin(pos, pr, d, p.theta, c, sn);
+      rope_cs[m][pr] = make_float2(c, sn);
+    }
+  };
+  if (table_early) fill_rope_table(0, static_cast<int>(p.m < MG ? p.m : MG));
 
-  // Everything above touches only weights; from here on we read x and write
-  // caches, so wait for the previous kernel in the stream.
   if (p.pdl) {
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
   }
   if (blockIdx.x == 0)
     for (int64_t i = threadIdx.x; i < p.n_zero_words; i += blockDim.x) p.zero_words[i] = 0u;
-
-  const float gamma = *p.gamma[mat];
-  bool waited = !bulk;
   bool ok = true;
+  if (gains_bulk) {
+    ok = mbar_wait_bounded(&gbar, 0, p.err);
+  } else {
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) gin_s[i] = p.g_in[i];
+    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) {
+      gq_s[i] = p.g_q[i];
+      gk_s[i] = p.g_k[i];
+    }
+  }
+
+  bool waited = !bulk;
   uint16_t* leader_out = cluster.map_shared_rank(&head_out[0][0], 0);
 
-  for (int64_t m0 = 0; m0 < p.m; m0 += MG) {
+  int group = 0;
+  for (int64_t m0 = 0; m0 < p.m; m0 += MG, ++group) {
     const int mgv = static_cast<int>((p.m - m0) < MG ? (p.m - m0) : MG);
-    __syncthreads();
-    // ---- input RMSNorm (reference/decoder_attention.py:117-140), rows m0.. into x_smem
+    __syncthreads();  // staging buffers (and the RoPE table) are free again
+    if (leader && mat < 2 && !(table_early && group == 0)) fill_rope_table(m0, mgv);
+    if (!stage_to_smem(x_stage, p.x + m0 * k, static_cast<uint32_t>(mgv * k * 2), &xbar, group & 1, p.err))
+      ok = false;
+    // ---- input RMSNorm (reference/decoder_attention.py:117-140) of rows m0.. into x_smem
     for (int m = 0; m < mgv; ++m) {
-      const uint16_t* xr = p.x + (m0 + m) * k;
+      const uint16_t* xr = x_stage + static_cast<int64_t>(m) * k;
       double ss = 0.0;
       for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
         const float v = bf16_bits_to_f32(xr[i]);
@@ -132,14 +197,14 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
       const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
       for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
         const float v = bf16_bits_to_f32(xr[i]);
-        const uint16_t nb = f32_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_f32(p.g_in[i])));
+        const uint16_t nb = f32_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_f32(gin_s[i])));
         x_smem_store(x_smem, nc, m, i, bf16_bits_to_f32(nb));
         if (p.dbg_xnorm && blockIdx.x == 0) p.dbg_xnorm[(m0 + m) * k + i] = nb;
       }
       __syncthreads();
     }
     if (!waited) {
-      ok = mbar_wait_bounded(&bars[warp], 0, p.err);
+      ok = mbar_wait_bounded(&bars[warp], 0, p.err) && ok;
       waited = true;
     }
     float acc[RPW][MG];
@@ -153,7 +218,7 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
               ok ? f32_to_bf16_bits(__fmul_rn(acc[r][m], gamma)) : uint16_t(0x7fc0);
     cluster.sync();
 
-    if (rank == 0 && warp < mgv) {
+    if (leader && warp < mgv) {
       // ---- head epilogue for activation row m0 + warp
       const int64_t mrow = m0 + warp;
       const int64_t b = mrow / p.tokens, t = mrow % p.tokens;
@@ -170,7 +235,7 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
           if (p.dbg_v) p.dbg_v[mrow * p.kv_heads * d + head * d + e] = y[e];
         }
       } else {
-        const uint16_t* g = (mat == 0) ? p.g_q : p.g_k;
+        const uint16_t* g = (mat == 0) ? gq_s : gk_s;
         double ss = 0.0;
         for (int64_t e = lane; e < d; e += 32) {
           const float v = bf16_bits_to_f32(y[e]);
@@ -200,9 +265,8 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
           }
           uint16_t r0 = n0, r1 = n1;
           if (pos != 0) {
-            float c, s;
-            rope_cos_sin(pos, pr, d, p.theta, c, s);
-            rope_pair(bf16_bits_to_f32(n0), bf16_bits_to_f32(n1), c, s, r0, r1);
+            const float2 cs = rope_cs[warp][pr];
+            rope_pair(bf16_bits_to_f32(n0), bf16_bits_to_f32(n1), cs.x, cs.y, r0, r1);
           }
           if (dst) {
             dst[e] = r0;
