@@ -8,18 +8,22 @@
 //
 // Work decomposition: one CTA per (split, kv head x head group, b*T + t).  The
 // CTA's GH query heads share every K/V row it loads.  Four warps walk the
-// split's positions in chunks of NPOS = 32/GH rows; lane l holds elements
-// [l*EPL, l*EPL+EPL) of q, k and v.  Per chunk the NPOS x GH partial dot
-// products are summed across lanes with a butterfly reduce-scatter (31
+// split's positions in chunks of NPOS = min(8, 32/GH) rows; lane l holds
+// elements [l*EPL, l*EPL+EPL) of q, k and v.  Per chunk the NPOS x GH partial
+// dot products are summed across lanes with a butterfly reduce-scatter (31
 // shuffles), after which lane l owns the score of (row l/GH, head l%GH).
-// Softmax is online (running max and sum per head, FP32).  Partial (m, l, o)
-// of every split go to the workspace; the last CTA of a (b, t, head group) to
-// finish — detected with an atomic counter, no waiting — combines them with
-// the log-sum-exp rule and writes BF16 context.  No score or probability
+// Softmax is online (running max and sum per head, FP32).  Splits combine
+// with the log-sum-exp rule in one of two ways: when a (b, t, head group) has
+// at most 16 splits they form one thread-block cluster and combine through
+// distributed shared memory after a cluster barrier; otherwise every split
+// writes (m, l, o) to the workspace and the last CTA to finish — detected with
+// an atomic counter, no waiting — combines them.  No score or probability
 // tensor is materialised.
 #pragma once
 
 #include <math.h>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -40,9 +44,11 @@ struct AttnParams {
   int splits;
   int head_groups;  // (Hq/Hkv) / GH
   float scale;      // FP32(1/sqrt(D))
-  float* partials;  // [B*T*Hq][splits][D + 2]  (o[D], m, l)
+  float* partials;  // [B*T*Hq][splits][D + 2]  (o[D], m, l)   (global combine only)
   unsigned* counters;  // [B*T*Hkv*head_groups], zero on entry, left zero on exit
   int pdl;
+  int cluster_combine;  // 1: the `splits` CTAs of a (b, t, head group) form one
+                        // thread-block cluster and combine through DSMEM
 };
 
 template <int EPL>
@@ -98,7 +104,10 @@ __device__ __forceinline__ int64_t seq_past(const AttnParams& p, int64_t b) {
 
 template <int EPL, int GH>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) {
-  constexpr int NPOS = 32 / GH;
+  // Rows per warp chunk; NPOS * GH <= 32 dot products go through one
+  // butterfly (unused slots are zero).  Capped at 8 rows to bound registers.
+  constexpr int NPOS = (32 / GH) > 8 ? 8 : (32 / GH);
+  constexpr int NDOT = NPOS * GH;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int split = blockIdx.x;
@@ -110,6 +119,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   const int64_t d = p.head_dim;
   const int64_t group = p.q_heads / p.kv_heads;
   const int64_t h0 = static_cast<int64_t>(kvh) * group + static_cast<int64_t>(hg) * GH;
+
+  // This kernel reads nothing before its dependency wait that its dependent
+  // (the O projection, which prefetches only weights) writes, so it lets the
+  // dependent launch at once.
+  if (p.pdl) pdl_launch_dependents();
 
   // Keys 0 .. P_b + t; never read beyond the physical capacity, whatever a
   // device-side length says.
@@ -139,10 +153,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
       for (int e = 0; e < EPL; ++e) kr[j][e] = vr[j][e] = 0.0f;
     }
   }
-  if (p.pdl) {
-    pdl_wait();
-    pdl_launch_dependents();
-  }
+  if (p.pdl) pdl_wait();
 
   // q for GH heads, this lane's slice.
   float q[GH][EPL];
@@ -173,6 +184,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     }
     float dots[32];
 #pragma unroll
+    for (int i = NDOT; i < 32; ++i) dots[i] = 0.0f;
+#pragma unroll
     for (int j = 0; j < NPOS; ++j)
 #pragma unroll
       for (int g = 0; g < GH; ++g) {
@@ -184,7 +197,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     const float dot = reduce_scatter32(dots, lane);
     const int my_j = lane / GH;
     const int my_g = lane % GH;
-    const bool valid = (c0 + my_j) < s1;
+    const bool valid = lane < NDOT && (c0 + my_j) < s1;
     const float score = valid ? __fmul_rn(dot, p.scale) : -INFINITY;
     // chunk max per head (lanes sharing my_g)
     float cmax = score;
@@ -239,6 +252,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   // thread i handles element i of head g for i < d (loop over heads)
   float* part_base = p.partials;
   const bool single = (p.splits == 1);
+  __shared__ float cta_m[GH], cta_l[GH];
+  __shared__ float cta_o[GH][32 * EPL];
   for (int idx = threadIdx.x; idx < GH * 32 * EPL; idx += kAttnThreads) {
     const int g = idx / (32 * EPL);
     const int e = idx % (32 * EPL);
@@ -254,6 +269,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
         o = fmaf(sm_o[w][g][e], f, o);
       }
     }
+    if (p.cluster_combine) {
+      cta_o[g][e] = o;
+      if (e == 0) {
+        cta_m[g] = mx;
+        cta_l[g] = l;
+      }
+      continue;
+    }
     if (e >= d) continue;
     const int64_t row = bt * p.q_heads + h0 + g;
     if (single) {
@@ -268,6 +291,36 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     }
   }
   if (single) return;
+
+  if (p.cluster_combine) {
+    // ---- the splits of this (b, t, head group) are one cluster: combine the
+    // CTAs' (m, l, o) through distributed shared memory.  CTA r finalises a
+    // slice of the GH x D outputs.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int ns = static_cast<int>(cluster.num_blocks());
+    const int rank = static_cast<int>(cluster.block_rank());
+    cluster.sync();
+    const int total = GH * static_cast<int>(d);
+    const int per = (total + ns - 1) / ns;
+    for (int idx = rank * per + threadIdx.x; idx < total && idx < (rank + 1) * per; idx += kAttnThreads) {
+      const int g = idx / static_cast<int>(d);
+      const int e = idx % static_cast<int>(d);
+      float mx = -INFINITY;
+      for (int r = 0; r < ns; ++r) mx = fmaxf(mx, *cluster.map_shared_rank(&cta_m[g], r));
+      float l = 0.0f, o = 0.0f;
+      for (int r = 0; r < ns; ++r) {
+        const float mr = *cluster.map_shared_rank(&cta_m[g], r);
+        if (mr == -INFINITY) continue;
+        const float f = expf(mr - mx);
+        l = fmaf(*cluster.map_shared_rank(&cta_l[g], r), f, l);
+        o = fmaf(*cluster.map_shared_rank(&cta_o[g][e], r), f, o);
+      }
+      p.ctx[(bt * p.q_heads + h0 + g) * d + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
+    }
+    cluster.sync();  // keep this CTA's shared memory alive until its peers are done
+    return;
+  }
 
   // ---- last CTA of this (b, t, head group) combines all splits.
   __shared__ unsigned s_last;

@@ -84,21 +84,50 @@ cudaError_t ensure_smem(F* fn, uint32_t bytes) {
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
-                   Args&&... args) {
+cudaError_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           bool pdl, unsigned cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
   if (pdl) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
   }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                   Args&&... args) {
+  return launch_cluster(kernel, grid, block, smem, stream, pdl, 1u, std::forward<Args>(args)...);
+}
+
+// Allow cluster sizes above the portable 8 for `fn` on the current device once.
+std::map<std::pair<const void*, int>, bool> g_cluster_set;
+
+template <typename F>
+cudaError_t ensure_big_clusters(F* fn) {
+  const void* key = reinterpret_cast<const void*>(fn);
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_smem_mutex);
+  if (g_cluster_set.count({key, dev})) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(key, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) g_cluster_set[{key, dev}] = true;
+  return e;
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -120,13 +149,24 @@ int check_weight(const nvfp4da_weight* w, const char* name) {
 
 // ---------------------------------------------------------------- GEMV plan
 struct GemvPlan {
-  int rpw, mg;
+  bool mma;      // tensor-core path (K % 32 == 0)
+  int rows;      // mma path: rows per CTA (16 or 32)
+  int rpw, mg;   // CUDA-core path
   uint32_t smem;
   int64_t ctas;
 };
 
 bool plan_gemv(int64_t m, int64_t n, int64_t k, GemvPlan& pl) {
   const int sms = sm_count();
+  if (mma_gemv_supported(k)) {
+    const int mg = static_cast<int>(m < kMmaMaxM ? m : kMmaMaxM);
+    const int rows = (ceil_div(n, 32) >= 2 * sms) ? 32 : 16;
+    const uint32_t bytes = mma_gemv_layout(rows, k, mg).total();
+    if (bytes <= kMaxDynSmem - 8 * 1024) {
+      pl = {true, rows, 0, 0, bytes, ceil_div(n, rows)};
+      return true;
+    }
+  }
   int rpw = 1;
   for (int r : {4, 2}) {
     if (ceil_div(n, kGemvWarps * r) >= sms) {
@@ -138,7 +178,7 @@ bool plan_gemv(int64_t m, int64_t n, int64_t k, GemvPlan& pl) {
   for (;;) {
     const uint32_t bytes = gemv_layout(kGemvWarps * rpw, k, mg).total();
     if (bytes <= kMaxDynSmem) {
-      pl = {rpw, mg, bytes, ceil_div(n, kGemvWarps * rpw)};
+      pl = {false, 0, rpw, mg, bytes, ceil_div(n, kGemvWarps * rpw)};
       return true;
     }
     if (mg > 1) mg >>= 1;
@@ -155,7 +195,16 @@ cudaError_t launch_gemv_t(const GemvParams& p, const GemvPlan& pl, cudaStream_t 
   return launch(k, dim3(static_cast<unsigned>(pl.ctas)), dim3(kGemvThreads), pl.smem, s, pdl, p);
 }
 
+template <int ROWS>
+cudaError_t launch_mma_gemv_t(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+  auto* k = mma_gemv_kernel<ROWS>;
+  cudaError_t e = ensure_smem(k, pl.smem);
+  if (e != cudaSuccess) return e;
+  return launch(k, dim3(static_cast<unsigned>(pl.ctas)), dim3(kMmaThreads), pl.smem, s, pdl, p);
+}
+
 cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+  if (pl.mma) return pl.rows == 32 ? launch_mma_gemv_t<32>(p, pl, s, pdl) : launch_mma_gemv_t<16>(p, pl, s, pdl);
 #define NVFP4DA_GEMV_CASE(R, M) \
   if (pl.rpw == R && pl.mg == M) return launch_gemv_t<R, M>(p, pl, s, pdl);
   NVFP4DA_GEMV_CASE(1, 1)
@@ -187,8 +236,11 @@ int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y,
 struct AttnPlan {
   int epl, gh, head_groups, splits;
   int64_t split_len;
+  bool cluster;  // splits combine through DSMEM as one cluster (2..16 splits)
   size_t partial_bytes, counter_bytes;
 };
+
+constexpr int kMaxAttnCluster = 16;
 
 bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                     int64_t max_past, AttnPlan& pl) {
@@ -204,7 +256,7 @@ bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_h
     }
   }
   const int64_t ng = group / gh;
-  const int64_t chunk = kAttnWarps * (32 / gh);
+  const int64_t chunk = kAttnWarps * std::min<int64_t>(8, 32 / gh);
   const int64_t visible = max_past + tokens;
   const int64_t base = batch * tokens * kv_heads * ng;
   int64_t splits = ceil_div(8LL * sm_count(), base);
@@ -224,14 +276,23 @@ bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_h
   pl.head_groups = static_cast<int>(ng);
   pl.splits = static_cast<int>(splits);
   pl.split_len = split_len;
-  pl.partial_bytes = splits > 1 ? align_up(static_cast<size_t>(batch * tokens * q_heads) * splits * (head_dim + 2) * 4, 256) : 0;
-  pl.counter_bytes = splits > 1 ? align_up(static_cast<size_t>(base) * 4, 256) : 0;
+  pl.cluster = splits > 1 && splits <= kMaxAttnCluster;
+  const bool global = splits > 1 && !pl.cluster;
+  pl.partial_bytes =
+      global ? align_up(static_cast<size_t>(batch * tokens * q_heads) * splits * (head_dim + 2) * 4, 256) : 0;
+  pl.counter_bytes = global ? align_up(static_cast<size_t>(base) * 4, 256) : 0;
   return true;
 }
 
 template <int EPL, int GH>
 cudaError_t launch_attn_t(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl) {
-  return launch(attn_split_kernel<EPL, GH>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+  auto* k = attn_split_kernel<EPL, GH>;
+  const unsigned cx = p.cluster_combine ? static_cast<unsigned>(p.splits) : 1u;
+  if (cx > 8) {
+    cudaError_t e = ensure_big_clusters(k);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_cluster(k, grid, dim3(kAttnThreads), 0, s, pdl, cx, p);
 }
 
 cudaError_t launch_attn(const AttnParams& p, const AttnPlan& pl, cudaStream_t s, bool pdl) {
@@ -284,7 +345,7 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
   if (!plan_attention(batch, tokens, q_heads, kv_heads, head_dim, max_past, pl))
     return fail(NVFP4DA_ERR_UNSUPPORTED, "head_dim %lld is not supported (need head_dim <= 256 and divisible by "
                 "its per-lane vector width)", static_cast<long long>(head_dim));
-  if (pl.partial_bytes + pl.counter_bytes > ws_bytes || (pl.splits > 1 && !ws))
+  if (pl.partial_bytes + pl.counter_bytes > ws_bytes || (pl.partial_bytes > 0 && !ws))
     return fail(NVFP4DA_ERR_WORKSPACE, "attention workspace too small (%zu < %zu bytes)", ws_bytes,
                 pl.partial_bytes + pl.counter_bytes);
   AttnParams p{};
@@ -304,10 +365,12 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
   p.splits = pl.splits;
   p.head_groups = pl.head_groups;
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)));
-  p.partials = pl.splits > 1 ? static_cast<float*>(ws) : nullptr;
-  p.counters = pl.splits > 1 ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pl.partial_bytes) : nullptr;
+  const bool global = pl.partial_bytes > 0;
+  p.partials = global ? static_cast<float*>(ws) : nullptr;
+  p.counters = global ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pl.partial_bytes) : nullptr;
   p.pdl = pdl ? 1 : 0;
-  if (clear_counters && pl.splits > 1) {
+  p.cluster_combine = pl.cluster ? 1 : 0;
+  if (clear_counters && global) {
     cudaError_t e = cudaMemsetAsync(p.counters, 0, pl.counter_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "attention counter clear");
   }
@@ -318,51 +381,38 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
 
 // ---------------------------------------------------------------- fused QKV plan
 struct QkvPlan {
-  int rpw, mg;
+  int rows;  // D / 4
+  int mg;
   uint32_t smem;
 };
 
 bool plan_qkv(int64_t m, int64_t hidden, int64_t head_dim, QkvPlan& pl) {
+  if (!mma_gemv_supported(hidden)) return false;
   if (head_dim % 32 != 0 || head_dim > kMaxHeadDim) return false;
-  const int rpw = static_cast<int>(head_dim / 32);
-  if (rpw != 1 && rpw != 2 && rpw != 4 && rpw != 8) return false;
-  int mg = m <= 1 ? 1 : (m == 2 ? 2 : 4);
-  for (;;) {
-    const uint32_t bytes = qkv_layout(kGemvWarps * rpw, hidden, head_dim, mg).total();
-    if (bytes <= kMaxDynSmem - 12 * 1024) {
-      pl = {rpw, mg, bytes};
-      return true;
-    }
-    if (mg == 1) return false;
-    mg >>= 1;
-  }
+  const int rows = static_cast<int>(head_dim / 4);
+  const int mg = static_cast<int>(m < kMmaMaxM ? m : kMmaMaxM);
+  const uint32_t bytes = qkv_layout(rows, hidden, head_dim, mg).total();
+  if (bytes > kMaxDynSmem - 16 * 1024) return false;
+  pl = {rows, mg, bytes};
+  return true;
 }
 
-template <int RPW, int MG>
+template <int ROWS>
 cudaError_t launch_qkv_t(const QkvParams& p, const QkvPlan& pl, int64_t units, cudaStream_t s, bool pdl) {
-  auto* k = qkv_fused_kernel<RPW, MG>;
+  auto* k = qkv_fused_kernel<ROWS>;
   cudaError_t e = ensure_smem(k, pl.smem);
   if (e != cudaSuccess) return e;
-  return launch(k, dim3(static_cast<unsigned>(units * kQkvCluster)), dim3(kGemvThreads), pl.smem, s, pdl, p);
+  return launch(k, dim3(static_cast<unsigned>(units * kQkvCluster)), dim3(kMmaThreads), pl.smem, s, pdl, p);
 }
 
 cudaError_t launch_qkv(const QkvParams& p, const QkvPlan& pl, int64_t units, cudaStream_t s, bool pdl) {
-#define NVFP4DA_QKV_CASE(R, M) \
-  if (pl.rpw == R && pl.mg == M) return launch_qkv_t<R, M>(p, pl, units, s, pdl);
-  NVFP4DA_QKV_CASE(1, 1)
-  NVFP4DA_QKV_CASE(1, 2)
-  NVFP4DA_QKV_CASE(1, 4)
-  NVFP4DA_QKV_CASE(2, 1)
-  NVFP4DA_QKV_CASE(2, 2)
-  NVFP4DA_QKV_CASE(2, 4)
-  NVFP4DA_QKV_CASE(4, 1)
-  NVFP4DA_QKV_CASE(4, 2)
-  NVFP4DA_QKV_CASE(4, 4)
-  NVFP4DA_QKV_CASE(8, 1)
-  NVFP4DA_QKV_CASE(8, 2)
-  NVFP4DA_QKV_CASE(8, 4)
-#undef NVFP4DA_QKV_CASE
-  return cudaErrorInvalidConfiguration;
+  switch (pl.rows) {
+    case 8: return launch_qkv_t<8>(p, pl, units, s, pdl);
+    case 16: return launch_qkv_t<16>(p, pl, units, s, pdl);
+    case 32: return launch_qkv_t<32>(p, pl, units, s, pdl);
+    case 64: return launch_qkv_t<64>(p, pl, units, s, pdl);
+    default: return cudaErrorInvalidConfiguration;
+  }
 }
 
 // ---------------------------------------------------------------- forward plan
@@ -689,13 +739,21 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* a, void* ws, s
   return NVFP4DA_OK;
 }
 
+#ifdef NVFP4DA_PHASES
+// Diagnostic build only: copy the phase table (CTA-major, 16 slots) to host.
+int nvfp4da_debug_phases(unsigned long long* host, size_t n) {
+  cudaError_t e = cudaMemcpyFromSymbol(host, g_phase_table, std::min(n, sizeof(g_phase_table)));
+  return e == cudaSuccess ? NVFP4DA_OK : cuda_fail(e, "phase table copy");
+}
+#endif
+
 int nvfp4da_qkv_rope_append(const nvfp4da_forward_args* a, uint16_t* q_rope_out, void* stream) {
   int r = check_forward(a);
   if (r) return r;
   if (!q_rope_out) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "q_rope_out is NULL");
   QkvPlan pl;
   if (!plan_qkv(a->batch * a->tokens, a->hidden, a->head_dim, pl))
-    return fail(NVFP4DA_ERR_UNSUPPORTED, "the fused QKV kernel needs head_dim %% 32 == 0 and head_dim <= 256");
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "the fused QKV kernel needs head_dim %% 32 == 0, head_dim <= 256 and hidden %% 32 == 0");
   QkvParams p = qkv_params(a, q_rope_out);
   const int64_t hq = a->hidden / a->head_dim;
   cudaError_t e = launch_qkv(p, pl, hq + 2 * a->kv_heads, static_cast<cudaStream_t>(stream), true);

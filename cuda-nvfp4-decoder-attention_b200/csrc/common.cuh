@@ -25,6 +25,30 @@ enum DeviceError : unsigned {
   kErrBarrierTimeout = 1u,
 };
 
+// ------------------------------------------------------------------ phase timing
+// Diagnostic build only (-DNVFP4DA_PHASES): thread 0 of each CTA records
+// clock64() at numbered points into a device table, read back by the debug
+// entry nvfp4da_debug_phases().  Compiled out of the normal library.
+#ifdef NVFP4DA_PHASES
+constexpr int kPhaseSlots = 16;
+constexpr int kPhaseCtas = 4096;
+__device__ unsigned long long g_phase_table[kPhaseCtas * kPhaseSlots];
+#define NVFP4DA_PHASE(i)                                                                               \
+  do {                                                                                                 \
+    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);              \
+    if (threadIdx.x == 0 && cta_ < kPhaseCtas) {                                                       \
+      unsigned long long t_;                                                                           \
+      if ((i) == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); else t_ = clock64();        \
+      g_phase_table[cta_ * kPhaseSlots + (i)] = t_;                                                    \
+      if ((i) == 0) g_phase_table[cta_ * kPhaseSlots + 15] = clock64();                                \
+    }                                                                                                  \
+  } while (0)
+#else
+#define NVFP4DA_PHASE(i) \
+  do {                   \
+  } while (0)
+#endif
+
 // ------------------------------------------------------------------ BF16
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);

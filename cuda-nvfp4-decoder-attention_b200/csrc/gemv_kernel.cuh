@@ -3,6 +3,7 @@
 #pragma once
 
 #include "gemv_core.cuh"
+#include "gemv_mma.cuh"
 
 namespace nvfp4da {
 
@@ -36,6 +37,7 @@ __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) 
   uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + lay.xs_off());
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  NVFP4DA_PHASE(0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemvWarps; ++i) mbar_init(&bars[i], 1);
@@ -48,6 +50,7 @@ __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) 
   const bool bulk = gemv_bulk_ok(p.packed, p.scales, k);
   gemv_stage_weights(w_smem, s_smem, p.packed, p.scales, k, row0, kRows, p.n, bulk, bars);
   const float gamma = *p.gamma;
+  NVFP4DA_PHASE(1);
   if (p.pdl) {
     pdl_wait();
     pdl_launch_dependents();
@@ -59,13 +62,16 @@ __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) 
     __syncthreads();  // staging buffers are free again
     if (!stage_to_smem(x_stage, p.x + m0 * k, static_cast<uint32_t>(mgv * k * 2), &xbar, group & 1, p.err))
       return;
+    NVFP4DA_PHASE(2);
     for (int64_t i = threadIdx.x; i < static_cast<int64_t>(mgv) * k; i += blockDim.x)
       x_smem_store(x_smem, nc, static_cast<int>(i / k), i % k, bf16_bits_to_f32(x_stage[i]));
     __syncthreads();
+    NVFP4DA_PHASE(3);
     if (!waited) {
       if (!mbar_wait_bounded(&bars[warp], 0, p.err)) return;
       waited = true;
     }
+    NVFP4DA_PHASE(4);
     float acc[RPW][MG];
     gemv_warp_rows<RPW, MG>(w_smem, s_smem, x_smem, k, mgv, acc);
 #pragma unroll
@@ -77,6 +83,73 @@ __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) 
           p.y[(m0 + m) * p.n + row] = f32_to_bf16_bits(__fmul_rn(acc[r][m], gamma));
       }
   }
+  NVFP4DA_PHASE(5);
+}
+
+// Tensor-core decode GEMV (K % 32 == 0): one CTA = ROWS weight rows, all M
+// activation rows in groups of up to 8 (the MMA's n dimension).
+template <int ROWS>
+__global__ void __launch_bounds__(kMmaThreads) mma_gemv_kernel(GemvParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ uint64_t wbar, xbar;
+  __shared__ float escale[kMmaMaxM];
+  __shared__ float red_small[kMmaMaxM * kMmaWarps];
+  __shared__ float outv[ROWS * 8];
+  NVFP4DA_PHASE(0);
+  const int64_t k = p.k;
+  const int mg = static_cast<int>(p.m < kMmaMaxM ? p.m : kMmaMaxM);
+  const MmaGemvLayout L = mma_gemv_layout(ROWS, k, mg);
+  uint8_t* w_smem = smem + L.w_off();
+  uint8_t* s_smem = smem + L.s_off();
+  uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + L.xs_off());
+  __half* x16 = reinterpret_cast<__half*>(smem + L.x16_off());
+  float* red = reinterpret_cast<float*>(smem + L.red_off());
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * ROWS;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&wbar, 1);
+    mbar_init(&xbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Weights never depend on an earlier kernel: stream them before the
+  // programmatic-dependency wait.
+  const bool bulk = mma_stage_weights(w_smem, s_smem, L, p.packed, p.scales, k, row0, ROWS, p.n, &wbar);
+  const float gamma = *p.gamma;
+  NVFP4DA_PHASE(1);
+  if (p.pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+  bool waited = !bulk;
+  int group = 0;
+  for (int64_t m0 = 0; m0 < p.m; m0 += kMmaMaxM, ++group) {
+    const int mgv = static_cast<int>((p.m - m0) < kMmaMaxM ? (p.m - m0) : kMmaMaxM);
+    __syncthreads();  // staging buffers are free again
+    if (!stage_to_smem(x_stage, p.x + m0 * k, static_cast<uint32_t>(mgv * k * 2), &xbar, group & 1, p.err))
+      return;
+    NVFP4DA_PHASE(2);
+    const bool f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
+    NVFP4DA_PHASE(3);
+    if (!waited) {
+      if (!mbar_wait_bounded(&wbar, 0, p.err)) return;
+      waited = true;
+    }
+    NVFP4DA_PHASE(4);
+    if (f16)
+      mma_gemv_pass<true>(w_smem, s_smem, L, reinterpret_cast<const uint16_t*>(x16), k, ROWS, mgv, red, outv);
+    else
+      mma_gemv_pass<false>(w_smem, s_smem, L, x_stage, k, ROWS, mgv, red, outv);
+    for (int i = threadIdx.x; i < ROWS * mgv; i += blockDim.x) {
+      const int n = i / ROWS, r = i % ROWS;
+      const int64_t row = row0 + r;
+      if (row < p.n) {
+        const float v = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
+        p.y[(m0 + n) * p.n + row] = f32_to_bf16_bits(__fmul_rn(v, gamma));
+      }
+    }
+  }
+  NVFP4DA_PHASE(5);
 }
 
 }  // namespace nvfp4da

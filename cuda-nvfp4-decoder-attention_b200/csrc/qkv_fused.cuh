@@ -19,6 +19,7 @@
 
 #include "elementwise.cuh"
 #include "gemv_core.cuh"
+#include "gemv_mma.cuh"
 
 namespace nvfp4da {
 
@@ -55,10 +56,10 @@ struct QkvParams {
   int pdl;
 };
 
-// Dynamic shared memory of the fused kernel: the GEMV layout followed by the
-// input-norm gain [K] and the two head-norm gains [D] (BF16).
+// Dynamic shared memory of the fused kernel: the MMA-GEMV layout followed by
+// the input-norm gain [K] and the two head-norm gains [D] (BF16).
 struct QkvSmemLayout {
-  GemvSmemLayout g;
+  MmaGemvLayout g;
   uint32_t gin_bytes, gh_bytes;
   __host__ __device__ uint32_t gin_off() const { return g.total(); }
   __host__ __device__ uint32_t gq_off() const { return g.total() + gin_bytes; }
@@ -68,27 +69,34 @@ struct QkvSmemLayout {
 
 __host__ __device__ inline QkvSmemLayout qkv_layout(int rows, int64_t k, int64_t d, int mg) {
   QkvSmemLayout l;
-  l.g = gemv_layout(rows, k, mg);
-  l.gin_bytes = round16(static_cast<uint64_t>(k) * 2);
-  l.gh_bytes = round16(static_cast<uint64_t>(d) * 2);
+  l.g = mma_gemv_layout(rows, k, mg);
+  l.gin_bytes = r16(static_cast<uint64_t>(k) * 2);
+  l.gh_bytes = r16(static_cast<uint64_t>(d) * 2);
   return l;
 }
 
-template <int RPW, int MG>
-__global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThreads)
+// ROWS = D / 4 weight rows per CTA (the 4 CTAs of a cluster cover one head).
+template <int ROWS>
+__global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThreads)
     qkv_fused_kernel(QkvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t bars[kGemvWarps];
-  __shared__ uint64_t xbar, gbar;
-  __shared__ uint16_t head_out[MG][kMaxHeadDim];
-  __shared__ float2 rope_cs[MG][kMaxHeadDim / 2];
-  __shared__ double red[kGemvWarps];
-  constexpr int kRows = kGemvWarps * RPW;  // = D / 4
+  __shared__ uint64_t wbar, xbar, gbar;
+  __shared__ uint16_t head_out[kMmaMaxM][kMaxHeadDim];
+  __shared__ float2 rope_cs[kMmaMaxM][kMaxHeadDim / 2];
+  __shared__ double red[kMmaWarps];
+  __shared__ float escale[kMmaMaxM];
+  __shared__ float red_small[kMmaMaxM * kMmaWarps];
+  __shared__ float outv[ROWS * 8];
+  NVFP4DA_PHASE(0);
+  // Nothing the dependent attention kernel reads before its own dependency
+  // wait (cache rows below P_b, past lengths) is written here, so let it
+  // launch at once and prefetch while this kernel streams its weights.
+  if (p.pdl) pdl_launch_dependents();
 
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int64_t unit = blockIdx.x / kQkvCluster;
-  const int64_t d = p.head_dim, k = p.hidden, nc = k / 16;
+  const int64_t d = p.head_dim, k = p.hidden;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   int mat;
@@ -104,20 +112,22 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
     head = unit - p.q_heads - p.kv_heads;
   }
   const int64_t n_rows = (mat == 0 ? p.q_heads : p.kv_heads) * d;
-  const int64_t row0 = head * d + static_cast<int64_t>(rank) * kRows;
+  const int64_t row0 = head * d + static_cast<int64_t>(rank) * ROWS;
   const bool leader = (rank == 0);
+  const int mg = static_cast<int>(p.m < kMmaMaxM ? p.m : kMmaMaxM);
 
-  const QkvSmemLayout lay = qkv_layout(kRows, k, d, MG);
+  const QkvSmemLayout lay = qkv_layout(ROWS, k, d, mg);
   uint8_t* w_smem = smem + lay.g.w_off();
   uint8_t* s_smem = smem + lay.g.s_off();
-  float4* x_smem = reinterpret_cast<float4*>(smem + lay.g.x_off());
   uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + lay.g.xs_off());
+  __half* x16 = reinterpret_cast<__half*>(smem + lay.g.x16_off());
+  float* mred = reinterpret_cast<float*>(smem + lay.g.red_off());
   uint16_t* gin_s = reinterpret_cast<uint16_t*>(smem + lay.gin_off());
   uint16_t* gq_s = reinterpret_cast<uint16_t*>(smem + lay.gq_off());
   uint16_t* gk_s = reinterpret_cast<uint16_t*>(smem + lay.gk_off());
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kGemvWarps; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&wbar, 1);
     mbar_init(&xbar, 1);
     mbar_init(&gbar, 1);
     fence_mbar_init();
@@ -125,10 +135,8 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
   __syncthreads();
 
   // ---- Before the programmatic-dependency wait: everything that no earlier
-  // kernel writes (weights, gains, gamma, and the RoPE table when the
-  // positions are a host scalar).
-  const bool bulk = gemv_bulk_ok(p.packed[mat], p.scales[mat], k);
-  gemv_stage_weights(w_smem, s_smem, p.packed[mat], p.scales[mat], k, row0, kRows, n_rows, bulk, bars);
+  // kernel writes (gains first — they are needed first — then weights, gamma,
+  // and the RoPE table when the positions are a host scalar).
   const bool gains_bulk = aligned16(p.g_in) && aligned16(p.g_q) && aligned16(p.g_k) && (k * 2) % 16 == 0 &&
                           (d * 2) % 16 == 0;
   if (gains_bulk && threadIdx.x == 0) {
@@ -137,6 +145,9 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
     bulk_g2s(gq_s, p.g_q, static_cast<uint32_t>(d * 2), &gbar);
     bulk_g2s(gk_s, p.g_k, static_cast<uint32_t>(d * 2), &gbar);
   }
+  const bool bulk = mma_stage_weights(w_smem, s_smem, lay.g, p.packed[mat], p.scales[mat], k, row0, ROWS, n_rows,
+                                      &wbar);
+  NVFP4DA_PHASE(1);
   const float gamma = *p.gamma[mat];
   const bool table_early = leader && mat < 2 && p.past_lengths == nullptr;
   auto fill_rope_table = [&](int64_t m0, int mgv) {
@@ -151,38 +162,40 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
       rope_cs[m][pr] = make_float2(c, sn);
     }
   };
-  if (table_early) fill_rope_table(0, static_cast<int>(p.m < MG ? p.m : MG));
+  if (table_early) fill_rope_table(0, mg);
+  NVFP4DA_PHASE(2);
 
-  if (p.pdl) {
-    pdl_wait();
-    pdl_launch_dependents();
-  }
+  if (p.pdl) pdl_wait();
   if (blockIdx.x == 0)
     for (int64_t i = threadIdx.x; i < p.n_zero_words; i += blockDim.x) p.zero_words[i] = 0u;
   bool ok = true;
-  if (gains_bulk) {
-    ok = mbar_wait_bounded(&gbar, 0, p.err);
-  } else {
+  if (!gains_bulk) {
     for (int64_t i = threadIdx.x; i < k; i += blockDim.x) gin_s[i] = p.g_in[i];
     for (int64_t i = threadIdx.x; i < d; i += blockDim.x) {
       gq_s[i] = p.g_q[i];
       gk_s[i] = p.g_k[i];
     }
   }
-
+  bool gains_ready = !gains_bulk;
   bool waited = !bulk;
   uint16_t* leader_out = cluster.map_shared_rank(&head_out[0][0], 0);
+  NVFP4DA_PHASE(3);
 
   int group = 0;
-  for (int64_t m0 = 0; m0 < p.m; m0 += MG, ++group) {
-    const int mgv = static_cast<int>((p.m - m0) < MG ? (p.m - m0) : MG);
+  for (int64_t m0 = 0; m0 < p.m; m0 += kMmaMaxM, ++group) {
+    const int mgv = static_cast<int>((p.m - m0) < kMmaMaxM ? (p.m - m0) : kMmaMaxM);
     __syncthreads();  // staging buffers (and the RoPE table) are free again
     if (leader && mat < 2 && !(table_early && group == 0)) fill_rope_table(m0, mgv);
     if (!stage_to_smem(x_stage, p.x + m0 * k, static_cast<uint32_t>(mgv * k * 2), &xbar, group & 1, p.err))
       ok = false;
-    // ---- input RMSNorm (reference/decoder_attention.py:117-140) of rows m0.. into x_smem
+    if (!gains_ready) {
+      ok = mbar_wait_bounded(&gbar, 0, p.err) && ok;
+      gains_ready = true;
+    }
+    NVFP4DA_PHASE(4);
+    // ---- input RMSNorm (reference/decoder_attention.py:117-140), in place in x_stage
     for (int m = 0; m < mgv; ++m) {
-      const uint16_t* xr = x_stage + static_cast<int64_t>(m) * k;
+      uint16_t* xr = x_stage + static_cast<int64_t>(m) * k;
       double ss = 0.0;
       for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
         const float v = bf16_bits_to_f32(xr[i]);
@@ -193,30 +206,35 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
       __syncthreads();
       double tot = 0.0;
 #pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) tot += red[w];
+      for (int w = 0; w < kMmaWarps; ++w) tot += red[w];
       const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
       for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
         const float v = bf16_bits_to_f32(xr[i]);
         const uint16_t nb = f32_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_f32(gin_s[i])));
-        x_smem_store(x_smem, nc, m, i, bf16_bits_to_f32(nb));
+        xr[i] = nb;
         if (p.dbg_xnorm && blockIdx.x == 0) p.dbg_xnorm[(m0 + m) * k + i] = nb;
       }
       __syncthreads();
     }
+    const bool f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
+    NVFP4DA_PHASE(5);
     if (!waited) {
-      ok = mbar_wait_bounded(&bars[warp], 0, p.err) && ok;
+      ok = mbar_wait_bounded(&wbar, 0, p.err) && ok;
       waited = true;
     }
-    float acc[RPW][MG];
-    gemv_warp_rows<RPW, MG>(w_smem, s_smem, x_smem, k, mgv, acc);
-#pragma unroll
-    for (int r = 0; r < RPW; ++r)
-#pragma unroll
-      for (int m = 0; m < MG; ++m)
-        if (lane == ((r * MG + m) & 31) && m < mgv)
-          leader_out[m * kMaxHeadDim + rank * kRows + warp * RPW + r] =
-              ok ? f32_to_bf16_bits(__fmul_rn(acc[r][m], gamma)) : uint16_t(0x7fc0);
+    NVFP4DA_PHASE(6);
+    if (f16)
+      mma_gemv_pass<true>(w_smem, s_smem, lay.g, reinterpret_cast<const uint16_t*>(x16), k, ROWS, mgv, mred, outv);
+    else
+      mma_gemv_pass<false>(w_smem, s_smem, lay.g, x_stage, k, ROWS, mgv, mred, outv);
+    for (int i = threadIdx.x; i < ROWS * mgv; i += blockDim.x) {
+      const int n = i / ROWS, r = i % ROWS;
+      const float v = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
+      leader_out[n * kMaxHeadDim + rank * ROWS + r] = ok ? f32_to_bf16_bits(__fmul_rn(v, gamma)) : uint16_t(0x7fc0);
+    }
+    NVFP4DA_PHASE(7);
     cluster.sync();
+    NVFP4DA_PHASE(8);
 
     if (leader && warp < mgv) {
       // ---- head epilogue for activation row m0 + warp
@@ -275,7 +293,9 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kGemvThrea
         }
       }
     }
+    NVFP4DA_PHASE(9);
     cluster.sync();  // head_out is reused by the next activation group
+    NVFP4DA_PHASE(10);
   }
 }
 
