@@ -753,7 +753,7 @@ int nvfp4da_qkv_rope_append(const nvfp4da_forward_args* a, uint16_t* q_rope_out,
   if (!q_rope_out) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "q_rope_out is NULL");
   QkvPlan pl;
   if (!plan_qkv(a->batch * a->tokens, a->hidden, a->head_dim, pl))
-    return fail(NVFP4DA_ERR_UNSUPPORTED, "the fused QKV kernel needs head_dim %% 32 == 0, head_dim <= 256 and hidden %% 32 == 0");
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "the fused QKV kernel needs head_dim %% 32 == 0, head_dim <= 256 and hidden %% 128 == 0");
   QkvParams p = qkv_params(a, q_rope_out);
   const int64_t hq = a->hidden / a->head_dim;
   cudaError_t e = launch_qkv(p, pl, hq + 2 * a->kv_heads, static_cast<cudaStream_t>(stream), true);

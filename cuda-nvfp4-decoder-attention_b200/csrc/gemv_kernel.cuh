@@ -86,12 +86,14 @@ __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) 
   NVFP4DA_PHASE(5);
 }
 
-// Tensor-core decode GEMV (K % 32 == 0): one CTA = ROWS weight rows, all M
-// activation rows in groups of up to 8 (the MMA's n dimension).
+// Tensor-core decode GEMV (K % 128 == 0): one CTA = ROWS weight rows, all M
+// activation rows in groups of up to 8 (the MMA's n dimension).  Weights go
+// from HBM straight into registers (issued before the dependency wait); the
+// scales take one bulk copy; activations are loaded after the wait.
 template <int ROWS>
 __global__ void __launch_bounds__(kMmaThreads) mma_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t wbar, xbar;
+  __shared__ uint64_t sbar;
   __shared__ float escale[kMmaMaxM];
   __shared__ float red_small[kMmaMaxM * kMmaWarps];
   __shared__ float outv[ROWS * 8];
@@ -99,53 +101,57 @@ __global__ void __launch_bounds__(kMmaThreads) mma_gemv_kernel(GemvParams p) {
   const int64_t k = p.k;
   const int mg = static_cast<int>(p.m < kMmaMaxM ? p.m : kMmaMaxM);
   const MmaGemvLayout L = mma_gemv_layout(ROWS, k, mg);
-  uint8_t* w_smem = smem + L.w_off();
   uint8_t* s_smem = smem + L.s_off();
   uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + L.xs_off());
   __half* x16 = reinterpret_cast<__half*>(smem + L.x16_off());
   float* red = reinterpret_cast<float*>(smem + L.red_off());
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * ROWS;
+  const int valid_rows = static_cast<int>((p.n - row0) < ROWS ? (p.n - row0) : ROWS);
+  const uint8_t* packed_row0 = p.packed + row0 * (k / 2);
 
   if (threadIdx.x == 0) {
-    mbar_init(&wbar, 1);
-    mbar_init(&xbar, 1);
+    mbar_init(&sbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  // Weights never depend on an earlier kernel: stream them before the
-  // programmatic-dependency wait.
-  const bool bulk = mma_stage_weights(w_smem, s_smem, L, p.packed, p.scales, k, row0, ROWS, p.n, &wbar);
+  // Weights and scales never depend on an earlier kernel: put this CTA's
+  // slice in flight before the programmatic-dependency wait.
+  const bool sbulk = stage_scales(s_smem, p.scales, k, row0, valid_rows, &sbar);
+  const WarpSlice wsl = warp_slice(ROWS, k);
+  constexpr int NB = 4;  // weight steps in flight per warp
+  WeightRegs<NB> w;
+  issue_weight_batch<NB>(w, packed_row0, k, wsl.tile, wsl.s0, wsl.s1, valid_rows);
   const float gamma = *p.gamma;
   NVFP4DA_PHASE(1);
   if (p.pdl) {
     pdl_wait();
     pdl_launch_dependents();
   }
-  bool waited = !bulk;
-  int group = 0;
-  for (int64_t m0 = 0; m0 < p.m; m0 += kMmaMaxM, ++group) {
+  bool scales_ready = !sbulk;
+  for (int64_t m0 = 0; m0 < p.m; m0 += kMmaMaxM) {
     const int mgv = static_cast<int>((p.m - m0) < kMmaMaxM ? (p.m - m0) : kMmaMaxM);
     __syncthreads();  // staging buffers are free again
-    if (!stage_to_smem(x_stage, p.x + m0 * k, static_cast<uint32_t>(mgv * k * 2), &xbar, group & 1, p.err))
-      return;
+    if (m0 > 0) issue_weight_batch<NB>(w, packed_row0, k, wsl.tile, wsl.s0, wsl.s1, valid_rows);
+    load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
+    __syncthreads();
     NVFP4DA_PHASE(2);
     const bool f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
     NVFP4DA_PHASE(3);
-    if (!waited) {
-      if (!mbar_wait_bounded(&wbar, 0, p.err)) return;
-      waited = true;
+    if (!scales_ready) {
+      if (!mbar_wait_bounded(&sbar, 0, p.err)) return;
+      scales_ready = true;
     }
     NVFP4DA_PHASE(4);
     if (f16)
-      mma_gemv_pass<true>(w_smem, s_smem, L, reinterpret_cast<const uint16_t*>(x16), k, ROWS, mgv, red, outv);
+      mma_gemv_pass<true, NB>(w, packed_row0, s_smem, reinterpret_cast<const uint16_t*>(x16), k, ROWS, valid_rows,
+                              mgv, red, outv);
     else
-      mma_gemv_pass<false>(w_smem, s_smem, L, x_stage, k, ROWS, mgv, red, outv);
+      mma_gemv_pass<false, NB>(w, packed_row0, s_smem, x_stage, k, ROWS, valid_rows, mgv, red, outv);
     for (int i = threadIdx.x; i < ROWS * mgv; i += blockDim.x) {
       const int n = i / ROWS, r = i % ROWS;
-      const int64_t row = row0 + r;
-      if (row < p.n) {
+      if (r < valid_rows) {
         const float v = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
-        p.y[(m0 + n) * p.n + row] = f32_to_bf16_bits(__fmul_rn(v, gamma));
+        p.y[(m0 + n) * p.n + row0 + r] = f32_to_bf16_bits(__fmul_rn(v, gamma));
       }
     }
   }

@@ -1,33 +1,34 @@
-// W4A16 decode GEMV on the tensor cores, operands decoded in registers.
+// W4A16 decode GEMV on the tensor cores, weights streamed straight from HBM
+// into registers and decoded there.
 //
 // Semantics (reference/w4a16.py:11-59, src/w4a16.cu:79-151):
 //   y[m, n] = BF16( sum_k FP32(x[m, k]) * W_hat[n, k] ),  W_hat = (q * beta) * gamma.
 // Evaluated as  y = BF16( gamma * 2^-e_m * sum_k (q*beta)[n, k] * (x[m, k] * 2^e_m) )
-// with one warp-level mma.m16n8k16 (FP32 accumulate) per 16 rows x 16 k:
+// with warp-level mma.m16n8k16 (FP32 accumulate), 16 weight rows x 16 k each:
 //  * A = q * beta in f16: the E2M1 nibble pair is converted by the hardware
 //    (cvt.rn.f16x2.e2m1x2, exact) and multiplied by the UE4M3 block scale in
 //    f16 — exact, since q*beta has at most 6 significant bits and lies in
 //    [2^-10, 2688];
-//  * B = the activation row scaled by a power of two 2^e_m (chosen so its
-//    largest element lands in [2^14, 2^15)) in f16 — used only when every
-//    element converts exactly, which is checked; otherwise the same loop runs
-//    with bf16 operands (x exactly, q*beta exactly in bf16 as well).
-// Every product is therefore exact; only the FP32 summation order differs
-// from the reference.
+//  * B = the activation row scaled by a power of two 2^e_m (its largest
+//    element lands in [2^14, 2^15)) in f16 — used only when every element
+//    converts exactly, which is checked; otherwise the same loop runs with bf16
+//    operands (x exactly, q*beta exactly in bf16 as well).
+// Every product is exact; only the FP32 summation order differs from the
+// reference.
 //
-// k-permutation: the sum over k is order-free, so each lane's MMA "k slots"
-// are fed from the physical k that one ldmatrix (A, 16 rows x 32 k = 16 B per
-// row) and one 16-byte shared load (B) hand it: lane (g = lane/4, t = lane%4)
-// holds physical k = 8t .. 8t+7 of a 32-wide k chunk; k 8t..8t+3 go to the
-// first MMA's slots (2t, 2t+1, 2t+8, 2t+9) and 8t+4..8t+7 to the second's.
-//
-// Shared-memory layout (per CTA, R rows, up to MG <= 8 activation rows):
-//   w_smem [R][K/2 + 16]   nibbles; 16 B padding per row so the 8 rows an
-//                          ldmatrix reads fall into distinct banks
-//   s_smem [R][K/16 + 16]  UE4M3 scale bytes, padded likewise
-//   x_stage [MG][K] bf16   raw (or normalised) activation rows
-//   x16     [MG][K] f16    power-of-two-scaled activations
-//   red     [warps][16][8] FP32 partial tiles for the cross-warp k reduction
+// Data movement: a warp owns a 16-row tile and a slice of K.  K is walked in
+// "steps" of 128 (64 bytes per row).  In a step, lane (g = lane/4, t = lane%4)
+// loads 16 contiguous bytes — physical k = 128 s + 32 t .. +31 — of rows g and
+// g+8 with one 16-byte global load each, so a quad reads 64 contiguous bytes
+// of a row (whole sectors).  A warp issues the loads of a whole batch of steps
+// before it waits on any, and the first batch is issued before the kernel's
+// programmatic-dependency wait, so the CTA's slice is in flight at once.
+// Because the sum over k is order-free, word p (0..3) of the lane's 16 bytes
+// (k = 128 s + 32 t + 8 p .. +7) feeds MMA-pair p: k 8p+{0,1}, 8p+{2,3} go to
+// the MMA slots (2t, 2t+1), (2t+8, 2t+9) of the first MMA and 8p+{4..7} to the
+// second; the activation operand is read from shared memory at the same
+// physical k.  Block scales (one byte per 16 k) come from one bulk copy of the
+// CTA's rows.
 #pragma once
 
 #include "common.cuh"
@@ -37,15 +38,14 @@ namespace nvfp4da {
 constexpr int kMmaWarps = 8;
 constexpr int kMmaThreads = kMmaWarps * kWarp;
 constexpr int kMmaMaxM = 8;  // activation rows per MMA pass (the n dimension)
+constexpr int kStepK = 128;  // k per step
 
 struct MmaGemvLayout {
-  uint32_t w_stride, s_stride;  // padded row strides (bytes)
-  uint32_t w_bytes, s_bytes, xs_bytes, x16_bytes, red_bytes;
-  __host__ __device__ uint32_t w_off() const { return 0; }
-  __host__ __device__ uint32_t s_off() const { return w_bytes; }
-  __host__ __device__ uint32_t xs_off() const { return w_bytes + s_bytes; }
-  __host__ __device__ uint32_t x16_off() const { return w_bytes + s_bytes + xs_bytes; }
-  __host__ __device__ uint32_t red_off() const { return w_bytes + s_bytes + xs_bytes + x16_bytes; }
+  uint32_t s_bytes, xs_bytes, x16_bytes, red_bytes;
+  __host__ __device__ uint32_t s_off() const { return 0; }
+  __host__ __device__ uint32_t xs_off() const { return s_bytes; }
+  __host__ __device__ uint32_t x16_off() const { return s_bytes + xs_bytes; }
+  __host__ __device__ uint32_t red_off() const { return s_bytes + xs_bytes + x16_bytes; }
   __host__ __device__ uint32_t total() const { return red_off() + red_bytes; }
 };
 
@@ -53,102 +53,17 @@ __host__ __device__ inline uint32_t r16(uint64_t v) { return static_cast<uint32_
 
 __host__ __device__ inline MmaGemvLayout mma_gemv_layout(int rows, int64_t k, int mg) {
   MmaGemvLayout l;
-  l.w_stride = r16(static_cast<uint64_t>(k / 2)) + 16;
-  l.s_stride = r16(static_cast<uint64_t>(k / 16)) + 16;
-  const int tiles_rows = ((rows + 15) / 16) * 16;
-  l.w_bytes = l.w_stride * tiles_rows;
-  l.s_bytes = l.s_stride * tiles_rows;
+  const int tile_rows = ((rows + 15) / 16) * 16;
+  l.s_bytes = r16(static_cast<uint64_t>(tile_rows) * (k / 16));
   l.xs_bytes = r16(static_cast<uint64_t>(mg) * k * 2);
   l.x16_bytes = r16(static_cast<uint64_t>(mg) * k * 2);
   l.red_bytes = kMmaWarps * 16 * 8 * 4;
   return l;
 }
 
-// The tensor-core path handles K % 32 == 0; other K use the reference-order
+// The tensor-core path needs K % 128 == 0 (whole steps); other K use the
 // CUDA-core GEMV.
-__host__ __device__ inline bool mma_gemv_supported(int64_t k) { return k >= 32 && k % 32 == 0; }
-
-// ---------------------------------------------------------------- weight staging
-// Bulk-copy rows [row0, row0 + rows) into the padded layout: one copy per row
-// for the nibbles and one for the scales, all counted on `bar` (threads
-// 0..rows-1 issue).  Rows at or past n_rows are zero-filled by the fallback
-// and skipped (never stored) by the bulk path.  Fallback when an address or
-// size is not 16-byte granular: cooperative byte copy + __syncthreads.
-// Returns true when the bulk path was taken (caller waits on `bar`).
-__device__ __forceinline__ bool mma_stage_weights(uint8_t* w_smem, uint8_t* s_smem, const MmaGemvLayout& L,
-                                                  const uint8_t* packed, const uint8_t* scales, int64_t k,
-                                                  int64_t row0, int rows, int64_t n_rows, uint64_t* bar) {
-  const int64_t kb = k / 2, ks = k / 16;
-  const bool bulk = (kb % 16 == 0) && (ks % 16 == 0) && aligned16(packed) && aligned16(scales);
-  int64_t valid = n_rows - row0;
-  valid = valid < 0 ? 0 : (valid > rows ? rows : valid);
-  if (bulk) {
-    if (threadIdx.x == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(valid * (kb + ks)));
-    __syncthreads();  // expect_tx before any complete_tx can land
-    if (threadIdx.x < valid) {
-      const int r = threadIdx.x;
-      bulk_g2s(w_smem + r * L.w_stride, packed + (row0 + r) * kb, static_cast<uint32_t>(kb), bar);
-      bulk_g2s(s_smem + r * L.s_stride, scales + (row0 + r) * ks, static_cast<uint32_t>(ks), bar);
-    }
-    return true;
-  }
-  for (int64_t i = threadIdx.x; i < static_cast<int64_t>(rows) * kb; i += blockDim.x) {
-    const int64_t r = i / kb, c = i % kb;
-    w_smem[r * L.w_stride + c] = r < valid ? packed[(row0 + r) * kb + c] : uint8_t(0);
-  }
-  for (int64_t i = threadIdx.x; i < static_cast<int64_t>(rows) * ks; i += blockDim.x) {
-    const int64_t r = i / ks, c = i % ks;
-    s_smem[r * L.s_stride + c] = r < valid ? scales[(row0 + r) * ks + c] : uint8_t(0);
-  }
-  __syncthreads();
-  return false;
-}
-
-// ---------------------------------------------------------------- activation prep
-// From BF16 rows in x_stage ([mgv][K]) build the f16 operand rows in x16:
-// x16[m][k] = f16(x[m][k] * 2^e_m) with e_m putting max|x[m]| in [2^14, 2^15).
-// Returns (uniformly over the CTA) whether every element converted exactly;
-// `escale[m]` receives 2^-e_m.  Must be called by all threads.
-__device__ __forceinline__ bool mma_prepare_f16(const uint16_t* x_stage, __half* x16, int64_t k, int mgv,
-                                                float* escale /* [kMmaMaxM] smem */,
-                                                float* red /* >= kMmaMaxM * warps floats */) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nw = blockDim.x >> 5;
-  // per-row amax
-  for (int m = 0; m < mgv; ++m) {
-    float mx = 0.0f;
-    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) mx = fmaxf(mx, fabsf(bf16_bits_to_f32(x_stage[m * k + i])));
-    mx = warp_max_f32(mx);
-    if (lane == 0) red[m * nw + warp] = mx;
-  }
-  __syncthreads();
-  if (threadIdx.x < mgv) {
-    float mx = 0.0f;
-    for (int w = 0; w < nw; ++w) mx = fmaxf(mx, red[threadIdx.x * nw + w]);
-    // 2^e with mx * 2^e in [2^14, 2^15); exponent of mx from its bits.
-    int e = 0;
-    if (mx > 0.0f && isfinite(mx)) {
-      const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 127;  // floor(log2) for normals
-      e = 14 - (ex < -126 ? -126 : ex);
-      e = e > 126 ? 126 : (e < -126 ? -126 : e);
-    }
-    escale[threadIdx.x] = __uint_as_float(static_cast<uint32_t>(127 + e) << 23);   // 2^e
-  }
-  __syncthreads();
-  int inexact = 0;
-  for (int m = 0; m < mgv; ++m) {
-    const float sc = escale[m], inv = 1.0f / sc;  // powers of two: both exact
-    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
-      const float x = bf16_bits_to_f32(x_stage[m * k + i]);
-      const __half h = __float2half_rn(x * sc);
-      inexact |= (__half2float(h) * inv != x);  // round trip must give x back
-      x16[m * k + i] = h;
-    }
-  }
-  __syncthreads();  // escale reads done before it is overwritten below
-  if (threadIdx.x < mgv) escale[threadIdx.x] = 1.0f / escale[threadIdx.x];  // 2^-e, exact
-  return __syncthreads_or(inexact) == 0;
-}
+__host__ __device__ inline bool mma_gemv_supported(int64_t k) { return k >= kStepK && k % kStepK == 0; }
 
 // ---------------------------------------------------------------- MMA primitives
 __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -167,12 +82,6 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void ldmatrix_x2(uint32_t& r0, uint32_t& r1, const void* row_addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
-               : "=r"(r0), "=r"(r1)
-               : "r"(smem_u32(row_addr)));
-}
-
 // f16x2 (exact q*beta) -> bf16x2 (exact as well: <= 6 significant bits).
 __device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
   const __half2 hv = *reinterpret_cast<const __half2*>(&h);
@@ -185,76 +94,125 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   return *reinterpret_cast<const uint32_t*>(&r);
 }
 
-// One warp: 16-row tile `tile_row0` (CTA-local) x k32 chunks [c0, c1),
-// against activation rows (n = lane/4 < mgv) in `xop` (f16 or bf16 bits,
-// [mgv][K]).  Accumulates into d[4] (rows g, g+8; n = 2t, 2t+1).
-template <bool F16>
-__device__ __forceinline__ void mma_tile_partial(const uint8_t* w_smem, const uint8_t* s_smem,
-                                                 const MmaGemvLayout& L, const uint16_t* xop, int64_t k,
-                                                 int tile_row0, int64_t c0, int64_t c1, int mgv, float (&d)[4]) {
-  const int lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const uint8_t* arow = w_smem + (tile_row0 + (lane & 7) + ((lane >> 3) & 1) * 8) * L.w_stride;
-  const uint8_t* s0 = s_smem + (tile_row0 + g) * L.s_stride + (t >> 1);
-  const uint8_t* s1 = s0 + 8 * L.s_stride;
-  const bool has_n = g < mgv;
-  const uint16_t* xrow = xop + static_cast<int64_t>(has_n ? g : 0) * k + 8 * t;
-#pragma unroll 2
-  for (int64_t c = c0; c < c1; ++c) {
-    uint32_t r0, r1;
-    ldmatrix_x2(r0, r1, arow + c * 16);
-    uint4 xb = make_uint4(0u, 0u, 0u, 0u);
-    if (has_n) xb = *reinterpret_cast<const uint4*>(xrow + c * 32);
-    const uint32_t sc0 = s0[2 * c], sc1 = s1[2 * c];
-    // block scales as f16x2 (same value in both halves)
-    uint32_t b2_0, b2_1;
-    asm("{\n .reg .b16 lo;\n cvt.u16.u32 lo, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}" : "=r"(b2_0) : "r"(sc0));
-    asm("{\n .reg .b16 lo;\n cvt.u16.u32 lo, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}" : "=r"(b2_1) : "r"(sc1));
-    b2_0 = __byte_perm(b2_0, 0, 0x1010);
-    b2_1 = __byte_perm(b2_1, 0, 0x1010);
-    uint32_t q0[4], q1[4];  // row g / row g+8: nibble pairs (8t,8t+1) (8t+2,+3) (8t+4,+5) (8t+6,+7)
+// Canonical UE4M3 byte -> f16x2 with the scale in both halves.
+__device__ __forceinline__ uint32_t ue4m3_to_f16x2_dup(uint32_t code) {
+  uint32_t h;
+  asm("{\n .reg .b16 lo;\n cvt.u16.u32 lo, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}" : "=r"(h) : "r"(code & 0xffu));
+  return __byte_perm(h, 0, 0x1010);
+}
+
+// Streaming 16-byte global load that does not allocate in L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// ---------------------------------------------------------------- per-warp work
+// Warp geometry for a CTA of `rows` weight rows (<= 16 * tiles, tiles in
+// {1, 2, 4, 8}): warp w handles tile w / ksplit and steps [s0, s1).
+struct WarpSlice {
+  int tile;
+  int s0, s1;
+};
+
+__device__ __forceinline__ WarpSlice warp_slice(int rows, int64_t k) {
+  const int warp = threadIdx.x >> 5;
+  const int tiles = (rows + 15) / 16;
+  const int ksplit = kMmaWarps / tiles;
+  const int steps = static_cast<int>(k / kStepK);
+  const int per = (steps + ksplit - 1) / ksplit;
+  WarpSlice w;
+  w.tile = warp / ksplit;
+  w.s0 = (warp % ksplit) * per;
+  w.s1 = w.s0 + per < steps ? w.s0 + per : steps;
+  return w;
+}
+
+// This lane's weight registers for up to NB steps of its warp slice (rows g
+// and g+8 of the tile): the batch a warp keeps in flight at once.
+template <int NB>
+struct WeightRegs {
+  uint4 lo[NB], hi[NB];
+};
+
+// Issue (no wait) the loads for steps [s, min(s + NB, s_end)).  Rows at or
+// past `valid_rows` (CTA-local) read as zero.
+template <int NB>
+__device__ __forceinline__ void issue_weight_batch(WeightRegs<NB>& w, const uint8_t* packed_row0, int64_t k,
+                                                   int tile, int s, int s_end, int valid_rows) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int r_lo = tile * 16 + g, r_hi = r_lo + 8;
+  const int64_t kb = k / 2;
+  const uint8_t* plo = packed_row0 + r_lo * kb + 16 * t;
+  const uint8_t* phi = packed_row0 + r_hi * kb + 16 * t;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      q0[i] = hmul2_u32(e2m1x2_to_f16x2(r0 >> (8 * i)), b2_0);
-      q1[i] = hmul2_u32(e2m1x2_to_f16x2(r1 >> (8 * i)), b2_1);
-    }
-    if constexpr (F16) {
-      const uint32_t a_lo[4] = {q0[0], q1[0], q0[1], q1[1]};
-      const uint32_t a_hi[4] = {q0[2], q1[2], q0[3], q1[3]};
-      mma_f16(d, a_lo, xb.x, xb.y);
-      mma_f16(d, a_hi, xb.z, xb.w);
-    } else {
-      const uint32_t a_lo[4] = {f16x2_to_bf16x2(q0[0]), f16x2_to_bf16x2(q1[0]), f16x2_to_bf16x2(q0[1]),
-                                f16x2_to_bf16x2(q1[1])};
-      const uint32_t a_hi[4] = {f16x2_to_bf16x2(q0[2]), f16x2_to_bf16x2(q1[2]), f16x2_to_bf16x2(q0[3]),
-                                f16x2_to_bf16x2(q1[3])};
-      mma_bf16(d, a_lo, xb.x, xb.y);
-      mma_bf16(d, a_hi, xb.z, xb.w);
+  for (int i = 0; i < NB; ++i) {
+    const int st = s + i;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    w.lo[i] = (st < s_end && r_lo < valid_rows) ? ldg_stream(plo + st * 64) : z;
+    w.hi[i] = (st < s_end && r_hi < valid_rows) ? ldg_stream(phi + st * 64) : z;
+  }
+}
+
+// Consume a batch: decode in registers, 8 MMAs per step.  `xop` is the
+// activation operand ([mgv][K], f16 or bf16 bits) in shared memory; `s_smem`
+// the CTA's scale rows ([rows][K/16]).
+template <bool F16, int NB>
+__device__ __forceinline__ void mma_batch(const WeightRegs<NB>& w, const uint8_t* s_smem, const uint16_t* xop,
+                                          int64_t k, int tile, int s, int s_end, int mgv, float (&d)[4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int64_t ks = k / 16;
+  const uint8_t* sc_lo = s_smem + (tile * 16 + g) * ks + 2 * t;
+  const uint8_t* sc_hi = sc_lo + 8 * ks;
+  const bool has_n = g < mgv;
+  const uint16_t* xrow = xop + static_cast<int64_t>(has_n ? g : 0) * k + 32 * t;
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    const int st = s + i;
+    if (st >= s_end) break;
+    // scales of blocks 8 st + 2 t (+1) for rows g and g+8
+    const uint32_t s2lo = *reinterpret_cast<const uint16_t*>(sc_lo + 8 * st);
+    const uint32_t s2hi = *reinterpret_cast<const uint16_t*>(sc_hi + 8 * st);
+    const uint32_t blo[2] = {ue4m3_to_f16x2_dup(s2lo), ue4m3_to_f16x2_dup(s2lo >> 8)};
+    const uint32_t bhi[2] = {ue4m3_to_f16x2_dup(s2hi), ue4m3_to_f16x2_dup(s2hi >> 8)};
+    const uint32_t wl[4] = {w.lo[i].x, w.lo[i].y, w.lo[i].z, w.lo[i].w};
+    const uint32_t wh[4] = {w.hi[i].x, w.hi[i].y, w.hi[i].z, w.hi[i].w};
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      uint4 xb = make_uint4(0u, 0u, 0u, 0u);
+      if (has_n) xb = *reinterpret_cast<const uint4*>(xrow + st * kStepK + 8 * p);
+      uint32_t q0[4], q1[4];  // rows g / g+8: nibble pairs of word p
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        q0[j] = hmul2_u32(e2m1x2_to_f16x2(wl[p] >> (8 * j)), blo[p >> 1]);
+        q1[j] = hmul2_u32(e2m1x2_to_f16x2(wh[p] >> (8 * j)), bhi[p >> 1]);
+      }
+      if constexpr (F16) {
+        const uint32_t a_lo[4] = {q0[0], q1[0], q0[1], q1[1]};
+        const uint32_t a_hi[4] = {q0[2], q1[2], q0[3], q1[3]};
+        mma_f16(d, a_lo, xb.x, xb.y);
+        mma_f16(d, a_hi, xb.z, xb.w);
+      } else {
+        const uint32_t a_lo[4] = {f16x2_to_bf16x2(q0[0]), f16x2_to_bf16x2(q1[0]), f16x2_to_bf16x2(q0[1]),
+                                  f16x2_to_bf16x2(q1[1])};
+        const uint32_t a_hi[4] = {f16x2_to_bf16x2(q0[2]), f16x2_to_bf16x2(q1[2]), f16x2_to_bf16x2(q0[3]),
+                                  f16x2_to_bf16x2(q1[3])};
+        mma_bf16(d, a_lo, xb.x, xb.y);
+        mma_bf16(d, a_hi, xb.z, xb.w);
+      }
     }
   }
 }
 
-// Full CTA GEMV pass for `rows` (<= 16 * tiles) rows and mgv activation rows.
-// Warps are split as (tile, k-slice); partial tiles are summed through
-// `red`.  On return, out[r * 8 + n] (r < rows, n < mgv) holds the FP32 sum
-// for CTA-local row r and activation row n, before gamma and 2^-e scaling.
-// Must be called by all kMmaWarps warps.
-template <bool F16>
-__device__ __forceinline__ void mma_gemv_pass(const uint8_t* w_smem, const uint8_t* s_smem, const MmaGemvLayout& L,
-                                              const uint16_t* xop, int64_t k, int rows, int mgv, float* red,
-                                              float* out) {
+// Sum the warps' partial 16x8 tiles: out[r * 8 + n] for CTA-local row r.
+__device__ __forceinline__ void reduce_tiles(const float (&d)[4], int rows, float* red, float* out) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int tiles = (rows + 15) / 16;
-  const int ksplit = kMmaWarps / tiles;  // tiles in {1, 2, 4, 8}
-  const int tile = warp / ksplit, ks = warp % ksplit;
-  const int64_t nchunks = k / 32;
-  const int64_t per = (nchunks + ksplit - 1) / ksplit;
-  const int64_t c0 = ks * per;
-  const int64_t c1 = (c0 + per < nchunks) ? c0 + per : nchunks;
-  float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  if (c0 < c1) mma_tile_partial<F16>(w_smem, s_smem, L, xop, k, tile * 16, c0, c1, mgv, d);
-  // partial tile -> red[warp][16][8]
   const int g = lane >> 2, t = lane & 3;
+  const int tiles = (rows + 15) / 16;
+  const int ksplit = kMmaWarps / tiles;
   float* rw = red + warp * 128;
   rw[g * 8 + 2 * t] = d[0];
   rw[g * 8 + 2 * t + 1] = d[1];
@@ -262,13 +220,124 @@ __device__ __forceinline__ void mma_gemv_pass(const uint8_t* w_smem, const uint8
   rw[(g + 8) * 8 + 2 * t + 1] = d[3];
   __syncthreads();
   for (int i = threadIdx.x; i < tiles * 128; i += blockDim.x) {
-    const int tl = i / 128, e = i % 128;
+    const int tl = i >> 7, e = i & 127;
     float s = 0.0f;
     for (int w = 0; w < ksplit; ++w) s += red[(tl * ksplit + w) * 128 + e];
-    const int r = tl * 16 + e / 8;
-    if (r < rows) out[r * 8 + (e % 8)] = s;
+    const int r = tl * 16 + (e >> 3);
+    if (r < rows) out[r * 8 + (e & 7)] = s;
   }
   __syncthreads();
+}
+
+// One full pass: this warp's slice over all its steps (batches of NB, the
+// first batch already issued into `w` by the caller), then the cross-warp
+// reduction into out[r * 8 + n].
+template <bool F16, int NB>
+__device__ __forceinline__ void mma_gemv_pass(WeightRegs<NB>& w, const uint8_t* packed_row0, const uint8_t* s_smem,
+                                              const uint16_t* xop, int64_t k, int rows, int valid_rows, int mgv,
+                                              float* red, float* out) {
+  const WarpSlice ws = warp_slice(rows, k);
+  float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int s = ws.s0; s < ws.s1; s += NB) {
+    if (s != ws.s0) issue_weight_batch<NB>(w, packed_row0, k, ws.tile, s, ws.s1, valid_rows);
+    mma_batch<F16, NB>(w, s_smem, xop, k, ws.tile, s, ws.s1, mgv, d);
+  }
+  reduce_tiles(d, rows, red, out);
+}
+
+// ---------------------------------------------------------------- scales
+// Copy the CTA's scale rows ([rows][K/16], contiguous in global memory) into
+// shared memory: one bulk copy on `bar` when 16-byte granular (returns true;
+// the caller waits on `bar` phase 0), else a cooperative copy (returns false,
+// the data is visible after the caller's next __syncthreads).  Rows at or past
+// valid_rows are not copied.
+__device__ __forceinline__ bool stage_scales(uint8_t* s_smem, const uint8_t* scales, int64_t k, int64_t row0,
+                                             int valid_rows, uint64_t* bar) {
+  const int64_t ks = k / 16;
+  const uint32_t bytes = static_cast<uint32_t>(valid_rows * ks);
+  const uint8_t* src = scales + row0 * ks;
+  if (aligned16(src) && bytes % 16 == 0) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar, bytes);
+      if (bytes) bulk_g2s(s_smem, src, bytes, bar);
+    }
+    return true;
+  }
+  for (uint32_t i = threadIdx.x; i < bytes; i += blockDim.x) s_smem[i] = src[i];
+  return false;
+}
+
+// ---------------------------------------------------------------- activations
+// Global -> shared copy of n BF16 values with 16-byte loads (all threads).
+__device__ __forceinline__ void load_rows_lsu(uint16_t* dst, const uint16_t* src, int64_t n) {
+  if (aligned16(src) && n % 8 == 0) {
+    const int64_t nv = n / 8;
+    for (int64_t i = threadIdx.x; i < nv; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[i] = *reinterpret_cast<const uint4*>(src + 8 * i);
+  } else {
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+// From BF16 rows in x_stage ([mgv][K], K % 8 == 0) build the f16 operand rows
+// in x16: x16[m][k] = f16(x[m][k] * 2^e_m) with e_m putting max|x[m]| in
+// [2^14, 2^15).  Returns (uniformly over the CTA) whether every element
+// converted exactly; `escale[m]` receives 2^-e_m.  Must be called by all
+// threads; x_stage must be visible to all threads on entry.
+__device__ __forceinline__ bool mma_prepare_f16(const uint16_t* x_stage, __half* x16, int64_t k, int mgv,
+                                                float* escale /* [kMmaMaxM] smem */,
+                                                float* red /* >= kMmaMaxM * warps floats */) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int kv = static_cast<int>(k / 8);  // uint4 per row
+  for (int m = 0; m < mgv; ++m) {
+    const uint4* row = reinterpret_cast<const uint4*>(x_stage + m * k);
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < kv; i += blockDim.x) {
+      const uint4 v = row[i];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(w[j] << 16)), fabsf(__uint_as_float(w[j] & 0xffff0000u))));
+    }
+    mx = warp_max_f32(mx);
+    if (lane == 0) red[m * nw + warp] = mx;
+  }
+  __syncthreads();
+  if (threadIdx.x < mgv) {
+    float mx = 0.0f;
+    for (int w = 0; w < nw; ++w) mx = fmaxf(mx, red[threadIdx.x * nw + w]);
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+      const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 127;  // floor(log2) for normals
+      e = 14 - (ex < -126 ? -126 : ex);
+      e = e > 126 ? 126 : (e < -126 ? -126 : e);
+    }
+    escale[threadIdx.x] = __uint_as_float(static_cast<uint32_t>(127 + e) << 23);  // 2^e
+  }
+  __syncthreads();
+  int inexact = 0;
+  for (int m = 0; m < mgv; ++m) {
+    const float sc = escale[m], inv = 1.0f / sc;  // powers of two: both exact
+    const uint4* row = reinterpret_cast<const uint4*>(x_stage + m * k);
+    uint4* orow = reinterpret_cast<uint4*>(x16 + m * k);
+    for (int i = threadIdx.x; i < kv; i += blockDim.x) {
+      const uint4 v = row[i];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = __uint_as_float(w[j] << 16), b = __uint_as_float(w[j] & 0xffff0000u);
+        const __half2 h = __floats2half2_rn(a * sc, b * sc);
+        inexact |= (__low2float(h) * inv != a) | (__high2float(h) * inv != b);  // round trip gives x back
+        o[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      orow[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  __syncthreads();  // escale reads done before it is overwritten below
+  if (threadIdx.x < mgv) escale[threadIdx.x] = 1.0f / escale[threadIdx.x];  // 2^-e, exact
+  return __syncthreads_or(inexact) == 0;
 }
 
 }  // namespace nvfp4da

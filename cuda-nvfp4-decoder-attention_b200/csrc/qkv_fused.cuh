@@ -80,7 +80,7 @@ template <int ROWS>
 __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThreads)
     qkv_fused_kernel(QkvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t wbar, xbar, gbar;
+  __shared__ uint64_t sbar, gbar;
   __shared__ uint16_t head_out[kMmaMaxM][kMaxHeadDim];
   __shared__ float2 rope_cs[kMmaMaxM][kMaxHeadDim / 2];
   __shared__ double red[kMmaWarps];
@@ -113,11 +113,12 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
   }
   const int64_t n_rows = (mat == 0 ? p.q_heads : p.kv_heads) * d;
   const int64_t row0 = head * d + static_cast<int64_t>(rank) * ROWS;
+  const int valid_rows = static_cast<int>((n_rows - row0) < ROWS ? (n_rows - row0) : ROWS);
   const bool leader = (rank == 0);
   const int mg = static_cast<int>(p.m < kMmaMaxM ? p.m : kMmaMaxM);
+  const uint8_t* packed_row0 = p.packed[mat] + row0 * (k / 2);
 
   const QkvSmemLayout lay = qkv_layout(ROWS, k, d, mg);
-  uint8_t* w_smem = smem + lay.g.w_off();
   uint8_t* s_smem = smem + lay.g.s_off();
   uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + lay.g.xs_off());
   __half* x16 = reinterpret_cast<__half*>(smem + lay.g.x16_off());
@@ -127,16 +128,16 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
   uint16_t* gk_s = reinterpret_cast<uint16_t*>(smem + lay.gk_off());
 
   if (threadIdx.x == 0) {
-    mbar_init(&wbar, 1);
-    mbar_init(&xbar, 1);
+    mbar_init(&sbar, 1);
     mbar_init(&gbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
 
   // ---- Before the programmatic-dependency wait: everything that no earlier
-  // kernel writes (gains first — they are needed first — then weights, gamma,
-  // and the RoPE table when the positions are a host scalar).
+  // kernel writes.  Gains (needed first) and scales by bulk copy, the first
+  // batch of weight bytes into registers, gamma, and the RoPE table when the
+  // positions are a host scalar.
   const bool gains_bulk = aligned16(p.g_in) && aligned16(p.g_q) && aligned16(p.g_k) && (k * 2) % 16 == 0 &&
                           (d * 2) % 16 == 0;
   if (gains_bulk && threadIdx.x == 0) {
@@ -145,8 +146,11 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
     bulk_g2s(gq_s, p.g_q, static_cast<uint32_t>(d * 2), &gbar);
     bulk_g2s(gk_s, p.g_k, static_cast<uint32_t>(d * 2), &gbar);
   }
-  const bool bulk = mma_stage_weights(w_smem, s_smem, lay.g, p.packed[mat], p.scales[mat], k, row0, ROWS, n_rows,
-                                      &wbar);
+  const bool sbulk = stage_scales(s_smem, p.scales[mat], k, row0, valid_rows, &sbar);
+  const WarpSlice wsl = warp_slice(ROWS, k);
+  constexpr int NB = 6;  // weight steps in flight per warp
+  WeightRegs<NB> w;
+  issue_weight_batch<NB>(w, packed_row0, k, wsl.tile, wsl.s0, wsl.s1, valid_rows);
   NVFP4DA_PHASE(1);
   const float gamma = *p.gamma[mat];
   const bool table_early = leader && mat < 2 && p.past_lengths == nullptr;
@@ -177,56 +181,74 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
     }
   }
   bool gains_ready = !gains_bulk;
-  bool waited = !bulk;
+  bool scales_ready = !sbulk;
   uint16_t* leader_out = cluster.map_shared_rank(&head_out[0][0], 0);
   NVFP4DA_PHASE(3);
 
-  int group = 0;
-  for (int64_t m0 = 0; m0 < p.m; m0 += kMmaMaxM, ++group) {
+  const int kv8 = static_cast<int>(k / 8);
+  for (int64_t m0 = 0; m0 < p.m; m0 += kMmaMaxM) {
     const int mgv = static_cast<int>((p.m - m0) < kMmaMaxM ? (p.m - m0) : kMmaMaxM);
     __syncthreads();  // staging buffers (and the RoPE table) are free again
-    if (leader && mat < 2 && !(table_early && group == 0)) fill_rope_table(m0, mgv);
-    if (!stage_to_smem(x_stage, p.x + m0 * k, static_cast<uint32_t>(mgv * k * 2), &xbar, group & 1, p.err))
-      ok = false;
+    if (m0 > 0) issue_weight_batch<NB>(w, packed_row0, k, wsl.tile, wsl.s0, wsl.s1, valid_rows);
+    if (leader && mat < 2 && !(table_early && m0 == 0)) fill_rope_table(m0, mgv);
+    load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
     if (!gains_ready) {
       ok = mbar_wait_bounded(&gbar, 0, p.err) && ok;
       gains_ready = true;
     }
+    __syncthreads();
     NVFP4DA_PHASE(4);
     // ---- input RMSNorm (reference/decoder_attention.py:117-140), in place in x_stage
     for (int m = 0; m < mgv; ++m) {
-      uint16_t* xr = x_stage + static_cast<int64_t>(m) * k;
+      uint4* xr = reinterpret_cast<uint4*>(x_stage + static_cast<int64_t>(m) * k);
       double ss = 0.0;
-      for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
-        const float v = bf16_bits_to_f32(xr[i]);
-        ss += static_cast<double>(v * v);
+      for (int i = threadIdx.x; i < kv8; i += blockDim.x) {
+        const uint4 v = xr[i];
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = __uint_as_float(wv[j] << 16), b = __uint_as_float(wv[j] & 0xffff0000u);
+          ss += static_cast<double>(a * a) + static_cast<double>(b * b);
+        }
       }
       ss = warp_sum_f64(ss);
       if (lane == 0) red[warp] = ss;
       __syncthreads();
       double tot = 0.0;
 #pragma unroll
-      for (int w = 0; w < kMmaWarps; ++w) tot += red[w];
+      for (int ww = 0; ww < kMmaWarps; ++ww) tot += red[ww];
       const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
-      for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
-        const float v = bf16_bits_to_f32(xr[i]);
-        const uint16_t nb = f32_to_bf16_bits(__fmul_rn(__fmul_rn(v, inv), bf16_bits_to_f32(gin_s[i])));
-        xr[i] = nb;
-        if (p.dbg_xnorm && blockIdx.x == 0) p.dbg_xnorm[(m0 + m) * k + i] = nb;
+      const uint4* gv = reinterpret_cast<const uint4*>(gin_s);
+      for (int i = threadIdx.x; i < kv8; i += blockDim.x) {
+        const uint4 v = xr[i], gg = gv[i];
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w}, wg[4] = {gg.x, gg.y, gg.z, gg.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__fmul_rn(__uint_as_float(wv[j] << 16), inv),
+                                                         __uint_as_float(wg[j] << 16)));
+          const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__fmul_rn(__uint_as_float(wv[j] & 0xffff0000u), inv),
+                                                         __uint_as_float(wg[j] & 0xffff0000u)));
+          o[j] = lo | (hi << 16);
+        }
+        const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
+        xr[i] = nv;
+        if (p.dbg_xnorm && blockIdx.x == 0) reinterpret_cast<uint4*>(p.dbg_xnorm + (m0 + m) * k)[i] = nv;
       }
       __syncthreads();
     }
     const bool f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
     NVFP4DA_PHASE(5);
-    if (!waited) {
-      ok = mbar_wait_bounded(&wbar, 0, p.err) && ok;
-      waited = true;
+    if (!scales_ready) {
+      ok = mbar_wait_bounded(&sbar, 0, p.err) && ok;
+      scales_ready = true;
     }
     NVFP4DA_PHASE(6);
     if (f16)
-      mma_gemv_pass<true>(w_smem, s_smem, lay.g, reinterpret_cast<const uint16_t*>(x16), k, ROWS, mgv, mred, outv);
+      mma_gemv_pass<true, NB>(w, packed_row0, s_smem, reinterpret_cast<const uint16_t*>(x16), k, ROWS, valid_rows,
+                              mgv, mred, outv);
     else
-      mma_gemv_pass<false>(w_smem, s_smem, lay.g, x_stage, k, ROWS, mgv, mred, outv);
+      mma_gemv_pass<false, NB>(w, packed_row0, s_smem, x_stage, k, ROWS, valid_rows, mgv, mred, outv);
     for (int i = threadIdx.x; i < ROWS * mgv; i += blockDim.x) {
       const int n = i / ROWS, r = i % ROWS;
       const float v = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
