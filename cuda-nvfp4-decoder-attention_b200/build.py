@@ -53,7 +53,7 @@ def build_capi(force: bool = False, verbose_ptxas: bool = False) -> Path:
         return CAPI_SO
     LIB.mkdir(exist_ok=True)
     cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           "-cudart", "static", "-o", str(CAPI_SO), str(CSRC / "capi.cu")]
+           "-cudart", "static", "-o", str(CAPI_SO), str(CSRC / "capi.cu"), str(CSRC / "noalloc.cu")]
     if verbose_ptxas:
         cmd.insert(1, "-Xptxas=-v")
     _run(cmd)

@@ -544,6 +544,10 @@ QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
 
 using namespace nvfp4da;
 
+// Lets other translation units of this library report through
+// nvfp4da_last_error(); not exported.
+__attribute__((visibility("hidden"))) void nvfp4da_set_last_error(const char* msg) { g_last_error = msg; }
+
 extern "C" {
 
 const char* nvfp4da_last_error(void) { return g_last_error.c_str(); }

@@ -25,7 +25,7 @@ EXPORTED = (
     "nvfp4da_quantize_workspace_size", "nvfp4da_quantize_nvfp4", "nvfp4da_rms_norm", "nvfp4da_apply_rope",
     "nvfp4da_w4a16_linear", "nvfp4da_kv_cache_append", "nvfp4da_gqa_attention_workspace_size",
     "nvfp4da_gqa_attention_cached", "nvfp4da_forward_workspace_size", "nvfp4da_decoder_attention_forward",
-    "nvfp4da_qkv_rope_append",
+    "nvfp4da_qkv_rope_append", "nvfp4da_decoder_attention_forward_noalloc",
 )
 
 
@@ -85,6 +85,7 @@ def load() -> C.CDLL:
         "nvfp4da_forward_workspace_size": (sz, [C.POINTER(ForwardArgs)]),
         "nvfp4da_decoder_attention_forward": (C.c_int, [C.POINTER(ForwardArgs), vp, sz, vp]),
         "nvfp4da_qkv_rope_append": (C.c_int, [C.POINTER(ForwardArgs), vp, vp]),
+        "nvfp4da_decoder_attention_forward_noalloc": (C.c_int, [C.POINTER(ForwardArgs), vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -233,3 +234,8 @@ class Forward:
     def run_qkv(self, q_rope_out: torch.Tensor, stream=None) -> None:
         """Only the fused front half (norm, QKV, per-head norm, RoPE, append)."""
         _check(load().nvfp4da_qkv_rope_append(C.byref(self.args), _p(q_rope_out), _stream(stream)))
+
+    def run_noalloc(self, stream=None) -> None:
+        """The same forward through the allocation-free entry point (scratch
+        from the library's built-in device array instead of self.workspace)."""
+        _check(load().nvfp4da_decoder_attention_forward_noalloc(C.byref(self.args), _stream(stream)))

@@ -161,6 +161,22 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* wo
  * args->output are not used.  Needs head_dim % 32 == 0 and head_dim <= 256. */
 int nvfp4da_qkv_rope_append(const nvfp4da_forward_args* args, uint16_t* q_rope_out, void* stream);
 
+/* Allocation-free forward.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory (a fixed HBM budget reserved up
+ * front, a host whose allocator owns all device memory, or a context where an
+ * allocation would stall the stream).  Same arguments and results as
+ * nvfp4da_decoder_attention_forward, but the scratch memory comes from one
+ * NVFP4DA_NOALLOC_SCRATCH_BYTES (8 MiB) array built into the library, resident
+ * on every GPU that loads it until the process exits.  Calls needing more
+ * scratch than that are rejected with NVFP4DA_ERR_WORKSPACE before any launch.
+ * The first call on a device looks up that device's copy of the array
+ * (cudaGetSymbolAddress) with the device current; make that first call before
+ * any stream capture.  Allocates nothing.  All calls share the one array and
+ * it keeps the last call's contents, so calls that overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller. */
+#define NVFP4DA_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int nvfp4da_decoder_attention_forward_noalloc(const nvfp4da_forward_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
