@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   // This kernel reads nothing before its dependency wait that its dependent
   // (the O projection, which prefetches only weights) writes, so it lets the
   // dependent launch at once.
+  [[maybe_unused]] constexpr unsigned kPhaseBase = 1024;
+  NVFP4DA_PHASE(0);
   if (p.pdl) pdl_launch_dependents();
 
   // Keys 0 .. P_b + t; never read beyond the physical capacity, whatever a
@@ -153,7 +155,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
       for (int e = 0; e < EPL; ++e) kr[j][e] = vr[j][e] = 0.0f;
     }
   }
+  NVFP4DA_PHASE(1);
   if (p.pdl) pdl_wait();
+  NVFP4DA_PHASE(2);
 
   // q for GH heads, this lane's slice.
   float q[GH][EPL];
@@ -233,6 +237,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
       }
   }
 
+  NVFP4DA_PHASE(3);
   // ---- combine the four warps of this CTA
   __shared__ float sm_m[kAttnWarps][GH], sm_l[kAttnWarps][GH];
   __shared__ float sm_o[kAttnWarps][GH][32 * EPL];
@@ -249,44 +254,49 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     for (int e = 0; e < EPL; ++e) sm_o[warp][g][lane * EPL + e] = acc[g][e];
   __syncthreads();
 
+  // Per-head rescale factors of the four warps, computed once.
+  __shared__ float wf[kAttnWarps][GH], cta_m[GH], cta_l[GH];
+  if (threadIdx.x < GH) {
+    const int g = threadIdx.x;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, sm_m[w][g]);
+    float l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float f = (sm_m[w][g] == -INFINITY) ? 0.0f : expf(sm_m[w][g] - mx);
+      wf[w][g] = f;
+      l = fmaf(sm_l[w][g], f, l);
+    }
+    cta_m[g] = mx;
+    cta_l[g] = l;
+  }
+  __syncthreads();
+
   // thread i handles element i of head g for i < d (loop over heads)
   float* part_base = p.partials;
   const bool single = (p.splits == 1);
-  __shared__ float cta_m[GH], cta_l[GH];
   __shared__ float cta_o[GH][32 * EPL];
   for (int idx = threadIdx.x; idx < GH * 32 * EPL; idx += kAttnThreads) {
     const int g = idx / (32 * EPL);
     const int e = idx % (32 * EPL);
-    float mx = -INFINITY;
+    float o = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, sm_m[w][g]);
-    float l = 0.0f, o = 0.0f;
-    if (mx != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float f = (sm_m[w][g] == -INFINITY) ? 0.0f : expf(sm_m[w][g] - mx);
-        l = fmaf(sm_l[w][g], f, l);
-        o = fmaf(sm_o[w][g][e], f, o);
-      }
-    }
+    for (int w = 0; w < kAttnWarps; ++w) o = fmaf(sm_o[w][g][e], wf[w][g], o);
     if (p.cluster_combine) {
       cta_o[g][e] = o;
-      if (e == 0) {
-        cta_m[g] = mx;
-        cta_l[g] = l;
-      }
       continue;
     }
     if (e >= d) continue;
     const int64_t row = bt * p.q_heads + h0 + g;
     if (single) {
-      p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
+      p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, cta_l[g]));
     } else {
       float* dst = part_base + (row * p.splits + split) * (d + 2);
       dst[e] = o;
       if (e == 0) {
-        dst[d] = mx;
-        dst[d + 1] = l;
+        dst[d] = cta_m[g];
+        dst[d + 1] = cta_l[g];
       }
     }
   }
@@ -294,31 +304,54 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
 
   if (p.cluster_combine) {
     // ---- the splits of this (b, t, head group) are one cluster: combine the
-    // CTAs' (m, l, o) through distributed shared memory.  CTA r finalises a
-    // slice of the GH x D outputs.
+    // CTAs' (m, l, o) through distributed shared memory.  Every CTA first
+    // gathers all ranks' (m, l) (independent remote loads), turns them into
+    // rescale weights, then finalises its slice of the GH x D outputs with one
+    // independent remote load per rank and element.
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     const int ns = static_cast<int>(cluster.num_blocks());
     const int rank = static_cast<int>(cluster.block_rank());
+    __shared__ float rw[16][GH], rl[16][GH], head_inv_l[GH];
+    NVFP4DA_PHASE(4);
     cluster.sync();
+    NVFP4DA_PHASE(5);
+    for (int i = threadIdx.x; i < ns * GH; i += kAttnThreads) {
+      const int r = i / GH, g = i % GH;
+      rw[r][g] = *cluster.map_shared_rank(&cta_m[g], r);
+      rl[r][g] = *cluster.map_shared_rank(&cta_l[g], r);
+    }
+    __syncthreads();
+    if (threadIdx.x < GH) {
+      const int g = threadIdx.x;
+      float mx = -INFINITY;
+      for (int r = 0; r < ns; ++r) mx = fmaxf(mx, rw[r][g]);
+      float l = 0.0f;
+      for (int r = 0; r < ns; ++r) {
+        const float f = (rw[r][g] == -INFINITY) ? 0.0f : expf(rw[r][g] - mx);
+        rw[r][g] = f;
+        l = fmaf(rl[r][g], f, l);
+      }
+      head_inv_l[g] = l;
+    }
+    __syncthreads();
     const int total = GH * static_cast<int>(d);
     const int per = (total + ns - 1) / ns;
     for (int idx = rank * per + threadIdx.x; idx < total && idx < (rank + 1) * per; idx += kAttnThreads) {
       const int g = idx / static_cast<int>(d);
       const int e = idx % static_cast<int>(d);
-      float mx = -INFINITY;
-      for (int r = 0; r < ns; ++r) mx = fmaxf(mx, *cluster.map_shared_rank(&cta_m[g], r));
-      float l = 0.0f, o = 0.0f;
-      for (int r = 0; r < ns; ++r) {
-        const float mr = *cluster.map_shared_rank(&cta_m[g], r);
-        if (mr == -INFINITY) continue;
-        const float f = expf(mr - mx);
-        l = fmaf(*cluster.map_shared_rank(&cta_l[g], r), f, l);
-        o = fmaf(*cluster.map_shared_rank(&cta_o[g][e], r), f, o);
-      }
-      p.ctx[(bt * p.q_heads + h0 + g) * d + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
+      float vals[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) vals[r] = r < ns ? *cluster.map_shared_rank(&cta_o[g][e], r) : 0.0f;
+      float o = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 16; ++r)
+        if (r < ns) o = fmaf(vals[r], rw[r][g], o);
+      p.ctx[(bt * p.q_heads + h0 + g) * d + e] = f32_to_bf16_bits(__fdiv_rn(o, head_inv_l[g]));
     }
+    NVFP4DA_PHASE(6);
     cluster.sync();  // keep this CTA's shared memory alive until its peers are done
+    NVFP4DA_PHASE(7);
     return;
   }
 

@@ -72,13 +72,17 @@ std::map<std::pair<const void*, int>, uint32_t> g_smem_set;
 
 template <typename F>
 cudaError_t ensure_smem(F* fn, uint32_t bytes) {
-  if (bytes <= 48 * 1024) return cudaSuccess;
   const void* key = reinterpret_cast<const void*>(fn);
   const int dev = current_device();
   std::lock_guard<std::mutex> lock(g_smem_mutex);
   auto it = g_smem_set.find({key, dev});
   if (it != g_smem_set.end() && it->second >= bytes) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(key, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  // Prefer the largest shared-memory carve-out so that several CTAs (of this
+  // kernel and of the kernels chained after it) fit on one SM.
+  cudaError_t e = cudaFuncSetAttribute(key, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       static_cast<int>(cudaSharedmemCarveoutMaxShared));
+  if (e == cudaSuccess && bytes > 48 * 1024)
+    e = cudaFuncSetAttribute(key, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
   if (e == cudaSuccess) g_smem_set[{key, dev}] = bytes;
   return e;
 }
@@ -287,6 +291,8 @@ bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_h
 template <int EPL, int GH>
 cudaError_t launch_attn_t(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl) {
   auto* k = attn_split_kernel<EPL, GH>;
+  cudaError_t ec = ensure_smem(k, 0);
+  if (ec != cudaSuccess) return ec;
   const unsigned cx = p.cluster_combine ? static_cast<unsigned>(p.splits) : 1u;
   if (cx > 8) {
     cudaError_t e = ensure_big_clusters(k);
@@ -536,6 +542,30 @@ QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
     p.dbg_kn = st->k_normalized;
   }
   p.pdl = 1;
+  // RoPE cos/sin for positions past_length + t, t < min(T, kMaxRopeRows), on the
+  // host with the arithmetic of reference/decoder_attention.py:237-257: FP32
+  // exponent 2m/D, FP32 theta^exponent, FP32 angle = p / denominator, FP32
+  // cos / sin -- each transcendental evaluated in double and rounded once.
+  p.rope_rows = 0;
+  if (!a->past_lengths && a->tokens <= kMaxRopeRows && a->head_dim <= kMaxHeadDim) {
+    const int64_t d = a->head_dim;
+    for (int64_t t = 0; t < a->tokens; ++t) {
+      const int64_t pos = a->past_length + t;
+      for (int64_t m = 0; m < d / 2; ++m) {
+        float c = 1.0f, sn = 0.0f;
+        if (pos != 0) {
+          const float expo = static_cast<float>(2 * m) / static_cast<float>(d);
+          const float denom = static_cast<float>(std::pow(static_cast<double>(a->rope_theta),
+                                                          static_cast<double>(expo)));
+          const float angle = static_cast<float>(pos) / denom;
+          c = static_cast<float>(std::cos(static_cast<double>(angle)));
+          sn = static_cast<float>(std::sin(static_cast<double>(angle)));
+        }
+        p.rope_host[t][m] = make_float2(c, sn);
+      }
+    }
+    p.rope_rows = static_cast<int>(a->tokens);
+  }
   return p;
 }
 
@@ -744,6 +774,34 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* a, void* ws, s
 }
 
 #ifdef NVFP4DA_PHASES
+// Diagnostic build only: max co-resident clusters of the fused QKV kernel
+// (ROWS = 32) and of the attention kernel (EPL 4, GH 4) for a cluster size.
+int nvfp4da_debug_occupancy(int which, int cluster, int smem, int* out) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.dynamicSmemBytes = smem;
+  cudaError_t e;
+  if (which == 0) {
+    cfg.gridDim = dim3(144);
+    cfg.blockDim = dim3(kMmaThreads);
+    cfg.numAttrs = 0;  // compile-time cluster dims
+    ensure_smem(qkv_fused_kernel<32>, smem);
+    e = cudaOccupancyMaxActiveClusters(out, qkv_fused_kernel<32>, &cfg);
+  } else {
+    cfg.gridDim = dim3(cluster * 6);
+    cfg.blockDim = dim3(kAttnThreads);
+    if (cluster > 8) ensure_big_clusters(attn_split_kernel<4, 4>);
+    e = cudaOccupancyMaxActiveClusters(out, attn_split_kernel<4, 4>, &cfg);
+  }
+  return e == cudaSuccess ? 0 : cuda_fail(e, "occupancy");
+}
+
 // Diagnostic build only: copy the phase table (CTA-major, 16 slots) to host.
 int nvfp4da_debug_phases(unsigned long long* host, size_t n) {
   cudaError_t e = cudaMemcpyFromSymbol(host, g_phase_table, std::min(n, sizeof(g_phase_table)));

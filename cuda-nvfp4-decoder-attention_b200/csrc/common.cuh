@@ -31,11 +31,11 @@ enum DeviceError : unsigned {
 // entry nvfp4da_debug_phases().  Compiled out of the normal library.
 #ifdef NVFP4DA_PHASES
 constexpr int kPhaseSlots = 16;
-constexpr int kPhaseCtas = 4096;
+constexpr int kPhaseCtas = 4096;  // table rows; each kernel writes rows kPhaseBase + cta
 __device__ unsigned long long g_phase_table[kPhaseCtas * kPhaseSlots];
 #define NVFP4DA_PHASE(i)                                                                               \
   do {                                                                                                 \
-    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);              \
+    const unsigned cta_ = kPhaseBase + blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
     if (threadIdx.x == 0 && cta_ < kPhaseCtas) {                                                       \
       unsigned long long t_;                                                                           \
       if ((i) == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); else t_ = clock64();        \

@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) 
   uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + lay.xs_off());
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  [[maybe_unused]] constexpr unsigned kPhaseBase = 2048;
   NVFP4DA_PHASE(0);
 
   if (threadIdx.x == 0) {
@@ -91,12 +92,15 @@ __global__ void __launch_bounds__(kGemvThreads) w4a16_gemv_kernel(GemvParams p) 
 // from HBM straight into registers (issued before the dependency wait); the
 // scales take one bulk copy; activations are loaded after the wait.
 template <int ROWS>
-__global__ void __launch_bounds__(kMmaThreads) mma_gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kMmaThreads, 2) mma_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ uint64_t sbar;
+  __shared__ float redf[2 * kMmaWarps];
+  __shared__ double redd[2 * kMmaWarps];
   __shared__ float escale[kMmaMaxM];
   __shared__ float red_small[kMmaMaxM * kMmaWarps];
   __shared__ float outv[ROWS * 8];
+  [[maybe_unused]] constexpr unsigned kPhaseBase = 2048;
   NVFP4DA_PHASE(0);
   const int64_t k = p.k;
   const int mg = static_cast<int>(p.m < kMmaMaxM ? p.m : kMmaMaxM);
@@ -132,10 +136,17 @@ __global__ void __launch_bounds__(kMmaThreads) mma_gemv_kernel(GemvParams p) {
     const int mgv = static_cast<int>((p.m - m0) < kMmaMaxM ? (p.m - m0) : kMmaMaxM);
     __syncthreads();  // staging buffers are free again
     if (m0 > 0) issue_weight_batch<NB>(w, packed_row0, k, wsl.tile, wsl.s0, wsl.s1, valid_rows);
-    load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
-    __syncthreads();
     NVFP4DA_PHASE(2);
-    const bool f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
+    bool f16;
+    constexpr int NCH = 2;  // register path for K <= 4096
+    if ((k / 8) <= NCH * kMmaThreads && aligned16(p.x)) {
+      const uint4 none[NCH] = {};
+      f16 = prep_rows_regs<NCH, false>(p.x + m0 * k, k, mgv, none, 0.0f, x_stage, x16, escale, redf, redd, nullptr);
+    } else {
+      load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
+      __syncthreads();
+      f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
+    }
     NVFP4DA_PHASE(3);
     if (!scales_ready) {
       if (!mbar_wait_bounded(&sbar, 0, p.err)) return;

@@ -162,7 +162,7 @@ __device__ __forceinline__ void issue_weight_batch(WeightRegs<NB>& w, const uint
 // the CTA's scale rows ([rows][K/16]).
 template <bool F16, int NB>
 __device__ __forceinline__ void mma_batch(const WeightRegs<NB>& w, const uint8_t* s_smem, const uint16_t* xop,
-                                          int64_t k, int tile, int s, int s_end, int mgv, float (&d)[4]) {
+                                          int64_t k, int tile, int s, int s_end, int mgv, float (&d)[4][4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int64_t ks = k / 16;
   const uint8_t* sc_lo = s_smem + (tile * 16 + g) * ks + 2 * t;
@@ -193,15 +193,15 @@ __device__ __forceinline__ void mma_batch(const WeightRegs<NB>& w, const uint8_t
       if constexpr (F16) {
         const uint32_t a_lo[4] = {q0[0], q1[0], q0[1], q1[1]};
         const uint32_t a_hi[4] = {q0[2], q1[2], q0[3], q1[3]};
-        mma_f16(d, a_lo, xb.x, xb.y);
-        mma_f16(d, a_hi, xb.z, xb.w);
+        mma_f16(d[p], a_lo, xb.x, xb.y);  // one accumulator per word p: four
+        mma_f16(d[p], a_hi, xb.z, xb.w);  // independent MMA dependency chains
       } else {
         const uint32_t a_lo[4] = {f16x2_to_bf16x2(q0[0]), f16x2_to_bf16x2(q1[0]), f16x2_to_bf16x2(q0[1]),
                                   f16x2_to_bf16x2(q1[1])};
         const uint32_t a_hi[4] = {f16x2_to_bf16x2(q0[2]), f16x2_to_bf16x2(q1[2]), f16x2_to_bf16x2(q0[3]),
                                   f16x2_to_bf16x2(q1[3])};
-        mma_bf16(d, a_lo, xb.x, xb.y);
-        mma_bf16(d, a_hi, xb.z, xb.w);
+        mma_bf16(d[p], a_lo, xb.x, xb.y);
+        mma_bf16(d[p], a_hi, xb.z, xb.w);
       }
     }
   }
@@ -237,12 +237,15 @@ __device__ __forceinline__ void mma_gemv_pass(WeightRegs<NB>& w, const uint8_t* 
                                               const uint16_t* xop, int64_t k, int rows, int valid_rows, int mgv,
                                               float* red, float* out) {
   const WarpSlice ws = warp_slice(rows, k);
-  float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float d[4][4] = {};
   for (int s = ws.s0; s < ws.s1; s += NB) {
     if (s != ws.s0) issue_weight_batch<NB>(w, packed_row0, k, ws.tile, s, ws.s1, valid_rows);
     mma_batch<F16, NB>(w, s_smem, xop, k, ws.tile, s, ws.s1, mgv, d);
   }
-  reduce_tiles(d, rows, red, out);
+  float dsum[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dsum[i] = (d[0][i] + d[1][i]) + (d[2][i] + d[3][i]);
+  reduce_tiles(dsum, rows, red, out);
 }
 
 // ---------------------------------------------------------------- scales
@@ -337,6 +340,113 @@ __device__ __forceinline__ bool mma_prepare_f16(const uint16_t* x_stage, __half*
   }
   __syncthreads();  // escale reads done before it is overwritten below
   if (threadIdx.x < mgv) escale[threadIdx.x] = 1.0f / escale[threadIdx.x];  // 2^-e, exact
+  return __syncthreads_or(inexact) == 0;
+}
+
+// ---------------------------------------------------------------- register path
+// Activation rows straight from global memory through registers, for
+// K <= 8 * kMmaThreads * NCH: optional RMSNorm (reference
+// decoder_attention.py:117-140; the gain's 8-element chunks `gch` already in
+// registers), then the power-of-two f16 operand.  Per row: one block
+// reduction for the sum of squares (FP64, exact), one for the max.  Writes the
+// BF16 row to x_stage (the bf16 fallback operand and, if `dbg`, the stage
+// output) and the f16 row to x16; escale[m] = 2^-e_m.  Returns, uniformly over
+// the CTA, whether every conversion was exact (then x16 is the operand).
+// `x` must be readable coherently (written by an earlier kernel at most).
+template <int NCH, bool NORM>
+__device__ __forceinline__ bool prep_rows_regs(const uint16_t* x, int64_t k, int mgv, const uint4 (&gch)[NCH],
+                                               float eps, uint16_t* x_stage, __half* x16, float* escale,
+                                               float* redf /* 2 * warps */, double* redd /* 2 * warps */,
+                                               uint16_t* dbg) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int kv8 = static_cast<int>(k / 8);
+  int inexact = 0;
+  for (int m = 0; m < mgv; ++m) {
+    const int buf = (m & 1) * kMmaWarps;
+    uint4 v[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int idx = threadIdx.x + c * kMmaThreads;
+      v[c] = idx < kv8 ? *reinterpret_cast<const uint4*>(x + m * k + 8 * idx) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    if constexpr (NORM) {
+      double ss = 0.0;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const uint32_t wv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = __uint_as_float(wv[j] << 16), b = __uint_as_float(wv[j] & 0xffff0000u);
+          ss += static_cast<double>(a * a) + static_cast<double>(b * b);
+        }
+      }
+      ss = warp_sum_f64(ss);
+      if (lane == 0) redd[buf + warp] = ss;
+      __syncthreads();
+      double tot = 0.0;
+#pragma unroll
+      for (int w = 0; w < kMmaWarps; ++w) tot += redd[buf + w];
+      const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), eps);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const uint32_t wv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+        const uint32_t wg[4] = {gch[c].x, gch[c].y, gch[c].z, gch[c].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t lo = f32_to_bf16_bits(
+              __fmul_rn(__fmul_rn(__uint_as_float(wv[j] << 16), inv), __uint_as_float(wg[j] << 16)));
+          const uint32_t hi = f32_to_bf16_bits(
+              __fmul_rn(__fmul_rn(__uint_as_float(wv[j] & 0xffff0000u), inv), __uint_as_float(wg[j] & 0xffff0000u)));
+          o[j] = lo | (hi << 16);
+        }
+        v[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    float mx = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int idx = threadIdx.x + c * kMmaThreads;
+      if (idx < kv8) {
+        reinterpret_cast<uint4*>(x_stage + m * k)[idx] = v[c];
+        if (dbg) reinterpret_cast<uint4*>(dbg + m * k)[idx] = v[c];
+      }
+      const uint32_t wv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(wv[j] << 16)), fabsf(__uint_as_float(wv[j] & 0xffff0000u))));
+    }
+    mx = warp_max_f32(mx);
+    if (lane == 0) redf[buf + warp] = mx;
+    __syncthreads();
+    mx = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMmaWarps; ++w) mx = fmaxf(mx, redf[buf + w]);
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+      const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 127;  // floor(log2) for normals
+      e = 14 - (ex < -126 ? -126 : ex);
+      e = e > 126 ? 126 : (e < -126 ? -126 : e);
+    }
+    const float sc = __uint_as_float(static_cast<uint32_t>(127 + e) << 23);   // 2^e
+    const float isc = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e
+    if (threadIdx.x == 0) escale[m] = isc;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int idx = threadIdx.x + c * kMmaThreads;
+      if (idx >= kv8) continue;
+      const uint32_t wv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = __uint_as_float(wv[j] << 16), b = __uint_as_float(wv[j] & 0xffff0000u);
+        const __half2 h = __floats2half2_rn(a * sc, b * sc);
+        inexact |= (__low2float(h) * isc != a) | (__high2float(h) * isc != b);  // round trip gives x back
+        o[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      reinterpret_cast<uint4*>(x16 + m * k)[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
   return __syncthreads_or(inexact) == 0;
 }
 

@@ -27,6 +27,7 @@ namespace cg = cooperative_groups;
 
 constexpr int kQkvCluster = 4;
 constexpr int kMaxHeadDim = 256;
+constexpr int kMaxRopeRows = 8;
 
 struct QkvParams {
   const uint16_t* x;     // [M, H] bf16, M = B*T
@@ -54,6 +55,10 @@ struct QkvParams {
   int64_t n_zero_words;
   unsigned* err;
   int pdl;
+  // RoPE cos/sin per token index t < rope_rows, computed on the host when the
+  // positions are the scalar past_length + t (rope_rows == 0: on the device).
+  int rope_rows;
+  float2 rope_host[kMaxRopeRows][kMaxHeadDim / 2];
 };
 
 // Dynamic shared memory of the fused kernel: the MMA-GEMV layout followed by
@@ -77,7 +82,7 @@ __host__ __device__ inline QkvSmemLayout qkv_layout(int rows, int64_t k, int64_t
 
 // ROWS = D / 4 weight rows per CTA (the 4 CTAs of a cluster cover one head).
 template <int ROWS>
-__global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThreads)
+__global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThreads, 2)
     qkv_fused_kernel(QkvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ uint64_t sbar, gbar;
@@ -87,6 +92,9 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
   __shared__ float escale[kMmaMaxM];
   __shared__ float red_small[kMmaMaxM * kMmaWarps];
   __shared__ float outv[ROWS * 8];
+  __shared__ float redf[2 * kMmaWarps];
+  __shared__ double redd[2 * kMmaWarps];
+  [[maybe_unused]] constexpr unsigned kPhaseBase = 0;
   NVFP4DA_PHASE(0);
   // Nothing the dependent attention kernel reads before its own dependency
   // wait (cache rows below P_b, past lengths) is written here, so let it
@@ -162,11 +170,27 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
       const int64_t b = mrow / p.tokens, t = mrow % p.tokens;
       const int64_t pos = (p.past_lengths ? p.past_lengths[b] : p.past_length) + t;
       float c = 1.0f, sn = 0.0f;
-      if (pos != 0) rope_cos_sin(pos, pr, d, p.theta, c, sn);
+      if (t < p.rope_rows) {
+        const float2 cs = p.rope_host[t][pr];
+        c = cs.x;
+        sn = cs.y;
+      } else if (pos != 0) {
+        rope_cos_sin(pos, pr, d, p.theta, c, sn);
+      }
       rope_cs[m][pr] = make_float2(c, sn);
     }
   };
   if (table_early) fill_rope_table(0, mg);
+  // Register path for the activation rows (K <= 4096): the gain's chunks
+  // are constants, so load them now.
+  constexpr int NCH = 2;
+  const bool reg_path = (k / 8) <= NCH * kMmaThreads && aligned16(p.x) && aligned16(p.g_in);
+  uint4 gch[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int idx = threadIdx.x + c * kMmaThreads;
+    gch[c] = (reg_path && idx < k / 8) ? ldg_stream(p.g_in + 8 * idx) : make_uint4(0u, 0u, 0u, 0u);
+  }
   NVFP4DA_PHASE(2);
 
   if (p.pdl) pdl_wait();
@@ -191,53 +215,64 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
     __syncthreads();  // staging buffers (and the RoPE table) are free again
     if (m0 > 0) issue_weight_batch<NB>(w, packed_row0, k, wsl.tile, wsl.s0, wsl.s1, valid_rows);
     if (leader && mat < 2 && !(table_early && m0 == 0)) fill_rope_table(m0, mgv);
-    load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
-    if (!gains_ready) {
-      ok = mbar_wait_bounded(&gbar, 0, p.err) && ok;
-      gains_ready = true;
-    }
-    __syncthreads();
-    NVFP4DA_PHASE(4);
-    // ---- input RMSNorm (reference/decoder_attention.py:117-140), in place in x_stage
-    for (int m = 0; m < mgv; ++m) {
-      uint4* xr = reinterpret_cast<uint4*>(x_stage + static_cast<int64_t>(m) * k);
-      double ss = 0.0;
-      for (int i = threadIdx.x; i < kv8; i += blockDim.x) {
-        const uint4 v = xr[i];
-        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = __uint_as_float(wv[j] << 16), b = __uint_as_float(wv[j] & 0xffff0000u);
-          ss += static_cast<double>(a * a) + static_cast<double>(b * b);
-        }
+    bool f16;
+    if (reg_path) {
+      if (!gains_ready) {
+        ok = mbar_wait_bounded(&gbar, 0, p.err) && ok;
+        gains_ready = true;
       }
-      ss = warp_sum_f64(ss);
-      if (lane == 0) red[warp] = ss;
-      __syncthreads();
-      double tot = 0.0;
-#pragma unroll
-      for (int ww = 0; ww < kMmaWarps; ++ww) tot += red[ww];
-      const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
-      const uint4* gv = reinterpret_cast<const uint4*>(gin_s);
-      for (int i = threadIdx.x; i < kv8; i += blockDim.x) {
-        const uint4 v = xr[i], gg = gv[i];
-        const uint32_t wv[4] = {v.x, v.y, v.z, v.w}, wg[4] = {gg.x, gg.y, gg.z, gg.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__fmul_rn(__uint_as_float(wv[j] << 16), inv),
-                                                         __uint_as_float(wg[j] << 16)));
-          const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__fmul_rn(__uint_as_float(wv[j] & 0xffff0000u), inv),
-                                                         __uint_as_float(wg[j] & 0xffff0000u)));
-          o[j] = lo | (hi << 16);
-        }
-        const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
-        xr[i] = nv;
-        if (p.dbg_xnorm && blockIdx.x == 0) reinterpret_cast<uint4*>(p.dbg_xnorm + (m0 + m) * k)[i] = nv;
+      NVFP4DA_PHASE(4);
+      f16 = prep_rows_regs<NCH, true>(p.x + m0 * k, k, mgv, gch, p.eps, x_stage, x16, escale, redf, redd,
+                                      (p.dbg_xnorm && blockIdx.x == 0) ? p.dbg_xnorm + m0 * k : nullptr);
+    } else {
+      load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
+      if (!gains_ready) {
+        ok = mbar_wait_bounded(&gbar, 0, p.err) && ok;
+        gains_ready = true;
       }
       __syncthreads();
+      NVFP4DA_PHASE(4);
+      // ---- input RMSNorm (reference/decoder_attention.py:117-140), in place in x_stage
+      for (int m = 0; m < mgv; ++m) {
+        uint4* xr = reinterpret_cast<uint4*>(x_stage + static_cast<int64_t>(m) * k);
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < kv8; i += blockDim.x) {
+          const uint4 v = xr[i];
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float a = __uint_as_float(wv[j] << 16), b = __uint_as_float(wv[j] & 0xffff0000u);
+            ss += static_cast<double>(a * a) + static_cast<double>(b * b);
+          }
+        }
+        ss = warp_sum_f64(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        double tot = 0.0;
+#pragma unroll
+        for (int ww = 0; ww < kMmaWarps; ++ww) tot += red[ww];
+        const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
+        const uint4* gv = reinterpret_cast<const uint4*>(gin_s);
+        for (int i = threadIdx.x; i < kv8; i += blockDim.x) {
+          const uint4 v = xr[i], gg = gv[i];
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w}, wg[4] = {gg.x, gg.y, gg.z, gg.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__fmul_rn(__uint_as_float(wv[j] << 16), inv),
+                                                           __uint_as_float(wg[j] << 16)));
+            const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__fmul_rn(__uint_as_float(wv[j] & 0xffff0000u), inv),
+                                                           __uint_as_float(wg[j] & 0xffff0000u)));
+            o[j] = lo | (hi << 16);
+          }
+          const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
+          xr[i] = nv;
+          if (p.dbg_xnorm && blockIdx.x == 0) reinterpret_cast<uint4*>(p.dbg_xnorm + (m0 + m) * k)[i] = nv;
+        }
+        __syncthreads();
+      }
+      f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
     }
-    const bool f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
     NVFP4DA_PHASE(5);
     if (!scales_ready) {
       ok = mbar_wait_bounded(&sbar, 0, p.err) && ok;
@@ -316,7 +351,9 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
       }
     }
     NVFP4DA_PHASE(9);
-    cluster.sync();  // head_out is reused by the next activation group
+    // head_out is reused by the next activation group.  After the last group
+    // nothing reads another CTA's shared memory any more, so no barrier.
+    if (m0 + kMmaMaxM < p.m) cluster.sync();
     NVFP4DA_PHASE(10);
   }
 }
