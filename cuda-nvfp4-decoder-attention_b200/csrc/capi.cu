@@ -17,6 +17,7 @@
 #include "attention.cuh"
 #include "elementwise.cuh"
 #include "gemv_kernel.cuh"
+#include "decode_step.cuh"
 #include "qkv_fused.cuh"
 
 namespace nvfp4da {
@@ -81,7 +82,9 @@ cudaError_t ensure_smem(F* fn, uint32_t bytes) {
   // kernel and of the kernels chained after it) fit on one SM.
   cudaError_t e = cudaFuncSetAttribute(key, cudaFuncAttributePreferredSharedMemoryCarveout,
                                        static_cast<int>(cudaSharedmemCarveoutMaxShared));
-  if (e == cudaSuccess && bytes > 48 * 1024)
+  // The opt-in is needed whenever static + dynamic shared memory passes 48 KB,
+  // not only when the dynamic part alone does, so always declare it.
+  if (e == cudaSuccess && bytes > 0)
     e = cudaFuncSetAttribute(key, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
   if (e == cudaSuccess) g_smem_set[{key, dev}] = bytes;
   return e;
@@ -569,6 +572,278 @@ QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
   return p;
 }
 
+
+// ---------------------------------------------------------------- one-kernel decode step
+// Synchronisation slots of the step kernel: zero-initialised at load, left
+// zero by every completed launch.  One slot per (device, stream): launches on
+// one stream are ordered, so they never share a slot concurrently.
+constexpr int kStepSlots = 64;
+__device__ unsigned g_step_sync[kStepSlots][kStepSyncWords];
+// Scratch words of the bounded-wait probe (nvfp4da_debug_wait_timeout).
+__device__ unsigned g_probe_words[4];
+
+std::mutex g_slot_mutex;
+std::map<std::pair<int, uintptr_t>, int> g_slot_of;
+int g_slots_used[kMaxDevices] = {0};
+unsigned* g_slot_base[kMaxDevices] = {nullptr};
+
+unsigned* slot_base_for_device(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (!g_slot_base[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_step_sync) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    g_slot_base[dev] = static_cast<unsigned*>(ptr);
+  }
+  return g_slot_base[dev];
+}
+
+// The slot of `stream` on the current device (assigned on first use), or
+// nullptr when every slot is taken.
+unsigned* step_slot(cudaStream_t stream) {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_slot_mutex);
+  unsigned* base = slot_base_for_device(dev);
+  if (!base) return nullptr;
+  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
+  auto it = g_slot_of.find(key);
+  int slot;
+  if (it != g_slot_of.end()) {
+    slot = it->second;
+  } else {
+    if (g_slots_used[dev] >= kStepSlots) return nullptr;
+    slot = g_slots_used[dev]++;
+    g_slot_of[key] = slot;
+  }
+  return base + static_cast<size_t>(slot) * kStepSyncWords;
+}
+
+const void* step_kernel_ptr(int epl, int gh) {
+#define NVFP4DA_STEP_CASE(E, G) \
+  if (epl == E && gh == G) return reinterpret_cast<const void*>(decode_step_kernel<E, G>);
+  NVFP4DA_STEP_CASE(2, 1)
+  NVFP4DA_STEP_CASE(2, 2)
+  NVFP4DA_STEP_CASE(2, 4)
+  NVFP4DA_STEP_CASE(2, 8)
+  NVFP4DA_STEP_CASE(4, 1)
+  NVFP4DA_STEP_CASE(4, 2)
+  NVFP4DA_STEP_CASE(4, 4)
+  NVFP4DA_STEP_CASE(4, 8)
+  NVFP4DA_STEP_CASE(8, 1)
+  NVFP4DA_STEP_CASE(8, 2)
+  NVFP4DA_STEP_CASE(8, 4)
+  NVFP4DA_STEP_CASE(8, 8)
+#undef NVFP4DA_STEP_CASE
+  return nullptr;
+}
+
+struct StepPlan {
+  int epl, gh;
+  int rq, n_qkv, ro, ro_rows, n_o;
+  int splits, split_len, grid;
+  uint32_t smem;
+  uint32_t off_qs, off_qw, off_os, off_ow, off_kv, off_q, off_xs, off_x16, off_red;
+  size_t proj, ctx, partials, total;  // workspace offsets / bytes
+};
+
+// Static shared memory of a step-kernel instantiation (cached per device).
+std::map<std::pair<const void*, int>, size_t> g_static_smem;
+
+size_t static_smem(const void* fn) {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_smem_mutex);
+  auto it = g_static_smem.find({fn, dev});
+  if (it != g_static_smem.end()) return it->second;
+  cudaFuncAttributes fa{};
+  size_t v = 16 * 1024;  // conservative if the query fails
+  if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess) v = fa.sharedSizeBytes;
+  else cudaGetLastError();
+  g_static_smem[{fn, dev}] = v;
+  return v;
+}
+
+// The step kernel covers decode (T == 1) of up to 8 sequences with
+// hidden % 256 == 0, hidden <= 4096, head_dim in {64, 128, 256}, 1/2/4/8 query
+// heads per KV head, no stage outputs, and a K/V tile per split that fits in
+// shared memory.  Returns false (no error) otherwise.
+bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
+  if (a->tokens != 1 || a->batch > kMmaMaxM || a->stages) return false;
+  const int64_t k = a->hidden, d = a->head_dim, hkv = a->kv_heads, hq = k / d, nb = a->batch;
+  if (k % 256 != 0 || k / 8 > 2 * kStepThreads) return false;
+  if (d % 32 != 0 || d > kMaxHeadDim) return false;
+  const int epl = static_cast<int>(d / 32);
+  const int64_t group = hq / hkv;
+  if (group != 1 && group != 2 && group != 4 && group != 8) return false;
+  const void* fn = step_kernel_ptr(epl, static_cast<int>(group));
+  if (!fn) return false;
+  if (kSyncHeads + (hq + 2 * hkv) + nb * hkv > kStepSyncWords) return false;
+  const std::pair<const nvfp4da_weight*, int> ws[4] = {{&a->q_weight, 0}, {&a->k_weight, 1}, {&a->v_weight, 2},
+                                                       {&a->out_weight, 3}};
+  for (auto& w : ws)
+    if (!aligned(w.first->packed_values, 16) || !aligned(w.first->block_scales, 16)) return false;
+  if (!aligned(a->x, 16) || !aligned(a->input_norm_weight, 16) || !aligned(a->k_cache, 16) ||
+      !aligned(a->v_cache, 16) || !aligned(a->output, 16))
+    return false;
+  const int grid = sm_count();
+  const int64_t nqkv = (hq + 2 * hkv) * d;
+  int rq = 0;
+  for (int r : {16, 32, 64, 128}) {
+    if (d % r == 0 && ceil_div(nqkv, r) <= grid) {
+      rq = r;
+      break;
+    }
+  }
+  if (!rq) return false;
+  const int ro = static_cast<int>(ceil_div(k, grid));
+  int tiles = 1;
+  while (16 * tiles < ro) tiles <<= 1;
+  if (16 * tiles > kStepMaxRows) return false;
+  const int64_t bh = nb * hkv;
+  if (bh > grid) return false;
+  const int64_t visible = (a->past_lengths ? a->max_past_length : a->past_length) + 1;
+  int64_t splits = std::max<int64_t>(1, std::min<int64_t>(grid / bh, ceil_div(visible, 64)));
+  const int64_t split_len = ceil_div(ceil_div(visible, splits), 8) * 8;
+  splits = ceil_div(visible, split_len);
+  s.epl = epl;
+  s.gh = static_cast<int>(group);
+  s.rq = rq;
+  s.n_qkv = static_cast<int>(nqkv / rq);
+  s.ro = ro;
+  s.ro_rows = 16 * tiles;
+  s.n_o = static_cast<int>(ceil_div(k, ro));
+  s.splits = static_cast<int>(splits);
+  s.split_len = static_cast<int>(split_len);
+  s.grid = grid;
+  uint64_t off = 0;
+  auto take = [&](uint64_t bytes) {
+    const uint64_t o = off;
+    off += (bytes + 127) / 128 * 128;
+    return static_cast<uint32_t>(o);
+  };
+  const uint64_t ks = k / 16, kb = k / 2;
+  s.off_qs = take(rq * ks);
+  s.off_qw = take(rq * kb);
+  // Only the RO rows a CTA owns are stored; the MMA tiles read up to ro_rows
+  // rows, the rows past RO landing in the buffers that follow (in bounds,
+  // their outputs are discarded).
+  s.off_os = take(ro * ks);
+  s.off_ow = take(ro * kb);
+  const uint64_t tile = 2ull * split_len * d * 2, smo = 1ull * kStepWarps * group * d * 4,
+                 comb = 2ull * group * splits * 4;
+  s.off_kv = take(std::max(tile, std::max(smo, comb)));
+  s.off_q = take(group * d * 4);
+  s.off_xs = take(nb * k * 2);
+  s.off_x16 = take(nb * k * 2);
+  s.off_red = take(kMmaWarps * 128 * 4);
+  if (off + static_smem(fn) > kMaxDynSmem) return false;
+  if (s.off_ow + static_cast<uint64_t>(s.ro_rows) * kb > off) return false;
+  s.smem = static_cast<uint32_t>(off);
+  size_t w = 0;
+  s.proj = w;
+  w += align_up(static_cast<size_t>(nb * nqkv) * 2, 256);
+  s.ctx = w;
+  w += align_up(static_cast<size_t>(nb * k) * 2, 256);
+  s.partials = w;
+  if (splits > 1) w += align_up(static_cast<size_t>(nb * hq) * splits * (d + 2) * 4, 256);
+  s.total = w;
+  return true;
+}
+
+int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaStream_t stream) {
+  unsigned* slot = step_slot(stream);
+  if (!slot) return fail(NVFP4DA_ERR_UNSUPPORTED, "no free synchronisation slot for another stream");
+  StepParams p{};
+  p.x = a->x;
+  p.g_in = a->input_norm_weight;
+  const nvfp4da_weight* w4[4] = {&a->q_weight, &a->k_weight, &a->v_weight, &a->out_weight};
+  for (int i = 0; i < 4; ++i) {
+    p.packed[i] = w4[i]->packed_values;
+    p.scales[i] = w4[i]->block_scales;
+    p.gamma[i] = w4[i]->global_decode_scale;
+  }
+  p.g_q = a->q_norm_weight;
+  p.g_k = a->k_norm_weight;
+  p.k_cache = a->k_cache;
+  p.v_cache = a->v_cache;
+  p.out = a->output;
+  p.batch = a->batch;
+  p.hidden = a->hidden;
+  p.q_heads = a->hidden / a->head_dim;
+  p.kv_heads = a->kv_heads;
+  p.head_dim = a->head_dim;
+  p.capacity = a->capacity;
+  p.past_length = a->past_length;
+  p.past_lengths = a->past_lengths;
+  p.eps = a->rms_eps;
+  p.theta = a->rope_theta;
+  p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(a->head_dim)));
+  p.rq = pl.rq;
+  p.rq_rows = pl.rq;
+  p.n_qkv_blocks = pl.n_qkv;
+  p.ro = pl.ro;
+  p.ro_rows = pl.ro_rows;
+  p.n_o_blocks = pl.n_o;
+  p.splits = pl.splits;
+  p.split_len = pl.split_len;
+  char* base = static_cast<char*>(ws);
+  p.proj = reinterpret_cast<uint16_t*>(base + pl.proj);
+  p.ctx = reinterpret_cast<uint16_t*>(base + pl.ctx);
+  p.partials = reinterpret_cast<float*>(base + pl.partials);
+  p.sync = slot;
+  p.timeout_ns = 500ull * 1000 * 1000;
+  p.off_qs = pl.off_qs;
+  p.off_qw = pl.off_qw;
+  p.off_os = pl.off_os;
+  p.off_ow = pl.off_ow;
+  p.off_kv = pl.off_kv;
+  p.off_q = pl.off_q;
+  p.off_xs = pl.off_xs;
+  p.off_x16 = pl.off_x16;
+  p.off_red = pl.off_red;
+  // RoPE cos/sin at position past_length, the host arithmetic of qkv_params.
+  p.rope_host_ok = 0;
+  if (!a->past_lengths) {
+    const int64_t d = a->head_dim, pos = a->past_length;
+    for (int64_t m = 0; m < d / 2; ++m) {
+      float c = 1.0f, sn = 0.0f;
+      if (pos != 0) {
+        const float expo = static_cast<float>(2 * m) / static_cast<float>(d);
+        const float denom =
+            static_cast<float>(std::pow(static_cast<double>(a->rope_theta), static_cast<double>(expo)));
+        const float angle = static_cast<float>(pos) / denom;
+        c = static_cast<float>(std::cos(static_cast<double>(angle)));
+        sn = static_cast<float>(std::sin(static_cast<double>(angle)));
+      }
+      p.rope_host[m] = make_float2(c, sn);
+    }
+    p.rope_host_ok = 1;
+  }
+  const void* fn = step_kernel_ptr(pl.epl, pl.gh);
+  cudaError_t e = ensure_smem(fn, pl.smem);
+  if (e != cudaSuccess) return cuda_fail(e, "step kernel shared-memory opt-in");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA co-resident: the counters are waited on
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* kargs[] = {&p};
+  e = cudaLaunchKernelExC(&cfg, fn, kargs);
+  if (e != cudaSuccess) return cuda_fail(e, "decode step launch");
+  return NVFP4DA_OK;
+}
+
+// Bounded-wait probe: one CTA waits on a counter that nothing sets.
+__global__ void wait_probe_kernel(unsigned* words, unsigned long long timeout_ns) {
+  const int idx = 0;
+  cta_wait(words, &idx, 1, 1u, words + 1, timeout_ns);
+}
 }  // namespace
 }  // namespace nvfp4da
 
@@ -706,18 +981,38 @@ size_t nvfp4da_forward_workspace_size(const nvfp4da_forward_args* a) {
   if (check_forward(a)) return 0;
   ForwardLayout L;
   if (plan_forward(a, L)) return 0;
-  return L.total;
+  StepPlan sp;
+  return plan_step(a, sp) ? std::max(L.total, sp.total) : L.total;
+}
+
+int nvfp4da_forward_step_supported(const nvfp4da_forward_args* a) {
+  if (check_forward(a)) return 0;
+  StepPlan sp;
+  return plan_step(a, sp) ? 1 : 0;
 }
 
 int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* a, void* ws, size_t ws_bytes, void* stream) {
+  return nvfp4da_decoder_attention_forward_path(a, ws, ws_bytes, stream, NVFP4DA_PATH_AUTO);
+}
+
+int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* ws, size_t ws_bytes, void* stream,
+                                           int path) {
   int r = check_forward(a);
   if (r) return r;
+  if (path != NVFP4DA_PATH_AUTO && path != NVFP4DA_PATH_CHAIN && path != NVFP4DA_PATH_STEP)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "unknown forward path %d", path);
   ForwardLayout L;
   if ((r = plan_forward(a, L))) return r;
-  if (!ws || ws_bytes < L.total)
-    return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace too small (%zu < %zu bytes)", ws_bytes, L.total);
+  StepPlan sp;
+  const bool step_ok = path != NVFP4DA_PATH_CHAIN && plan_step(a, sp);
+  if (path == NVFP4DA_PATH_STEP && !step_ok)
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "the one-kernel decode step does not cover this configuration");
+  const size_t need = step_ok ? std::max(L.total, sp.total) : L.total;
+  if (!ws || ws_bytes < need)
+    return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace too small (%zu < %zu bytes)", ws_bytes, need);
   if (!aligned(ws, 256)) return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace must be 256-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (step_ok) return run_step(a, sp, ws, s);
   char* base = static_cast<char*>(ws);
   const nvfp4da_forward_stages* st = a->stages;
   const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens, d = a->head_dim;
@@ -771,6 +1066,31 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* a, void* ws, s
   }
   if ((r = run_gemv(ctx_buf, m, a->out_weight, a->output, s, L.fused))) return r;
   return NVFP4DA_OK;
+}
+
+int nvfp4da_forward_sync_status(void* stream, unsigned* flags, int clear) {
+  if (!flags) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "flags is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned* slot = step_slot(s);
+  if (!slot) return fail(NVFP4DA_ERR_UNSUPPORTED, "no synchronisation slot for this stream");
+  cudaError_t e = cudaMemcpyAsync(flags, slot + kSyncErr, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(slot + kSyncErr, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  return e == cudaSuccess ? NVFP4DA_OK : cuda_fail(e, "sync status read");
+}
+
+int nvfp4da_debug_wait_timeout(void* stream, unsigned long long timeout_ns, unsigned* flags) {
+  if (!flags) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "flags is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* words = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&words, g_probe_words);
+  if (e == cudaSuccess) e = cudaMemsetAsync(words, 0, sizeof(g_probe_words), s);
+  if (e != cudaSuccess) return cuda_fail(e, "probe setup");
+  wait_probe_kernel<<<1, 32, 0, s>>>(static_cast<unsigned*>(words), timeout_ns);
+  NVFP4DA_CHECK_LAUNCH("probe launch");
+  e = cudaMemcpyAsync(flags, static_cast<unsigned*>(words) + 1, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  return e == cudaSuccess ? NVFP4DA_OK : cuda_fail(e, "probe read");
 }
 
 #ifdef NVFP4DA_PHASES

@@ -248,6 +248,41 @@ __device__ __forceinline__ void mma_gemv_pass(WeightRegs<NB>& w, const uint8_t* 
   reduce_tiles(dsum, rows, red, out);
 }
 
+// The same pass with the CTA's weight rows already in shared memory
+// (`w_smem`: rows x K/2 bytes, row-major as in global memory), for kernels
+// that bulk-copy their whole weight slice at launch.
+template <int NB>
+__device__ __forceinline__ void load_weight_batch_smem(WeightRegs<NB>& w, const uint8_t* w_smem, int64_t k, int tile,
+                                                       int s, int s_end) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int64_t kb = k / 2;
+  const uint8_t* plo = w_smem + (tile * 16 + g) * kb + 16 * t;
+  const uint8_t* phi = plo + 8 * kb;
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    const int st = s + i;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    w.lo[i] = st < s_end ? *reinterpret_cast<const uint4*>(plo + st * 64) : z;
+    w.hi[i] = st < s_end ? *reinterpret_cast<const uint4*>(phi + st * 64) : z;
+  }
+}
+
+template <bool F16, int NB>
+__device__ __forceinline__ void mma_gemv_pass_smem(const uint8_t* w_smem, const uint8_t* s_smem, const uint16_t* xop,
+                                                   int64_t k, int rows, int mgv, float* red, float* out) {
+  const WarpSlice ws = warp_slice(rows, k);
+  float d[4][4] = {};
+  for (int s = ws.s0; s < ws.s1; s += NB) {
+    WeightRegs<NB> w;
+    load_weight_batch_smem<NB>(w, w_smem, k, ws.tile, s, ws.s1);
+    mma_batch<F16, NB>(w, s_smem, xop, k, ws.tile, s, ws.s1, mgv, d);
+  }
+  float dsum[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dsum[i] = (d[0][i] + d[1][i]) + (d[2][i] + d[3][i]);
+  reduce_tiles(dsum, rows, red, out);
+}
+
 // ---------------------------------------------------------------- scales
 // Copy the CTA's scale rows ([rows][K/16], contiguous in global memory) into
 // shared memory: one bulk copy on `bar` when 16-byte granular (returns true;
@@ -352,8 +387,10 @@ __device__ __forceinline__ bool mma_prepare_f16(const uint16_t* x_stage, __half*
 // BF16 row to x_stage (the bf16 fallback operand and, if `dbg`, the stage
 // output) and the f16 row to x16; escale[m] = 2^-e_m.  Returns, uniformly over
 // the CTA, whether every conversion was exact (then x16 is the operand).
-// `x` must be readable coherently (written by an earlier kernel at most).
-template <int NCH, bool NORM>
+// `x` must be readable coherently: written by an earlier kernel, or (with
+// L2_ONLY, which reads through L2 only) by another CTA of this kernel before a
+// release/acquire handshake.
+template <int NCH, bool NORM, bool L2_ONLY = false>
 __device__ __forceinline__ bool prep_rows_regs(const uint16_t* x, int64_t k, int mgv, const uint4 (&gch)[NCH],
                                                float eps, uint16_t* x_stage, __half* x16, float* escale,
                                                float* redf /* 2 * warps */, double* redd /* 2 * warps */,
@@ -367,7 +404,13 @@ __device__ __forceinline__ bool prep_rows_regs(const uint16_t* x, int64_t k, int
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int idx = threadIdx.x + c * kMmaThreads;
-      v[c] = idx < kv8 ? *reinterpret_cast<const uint4*>(x + m * k + 8 * idx) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4* src = reinterpret_cast<const uint4*>(x + m * k + 8 * idx);
+      if (idx >= kv8)
+        v[c] = make_uint4(0u, 0u, 0u, 0u);
+      else if constexpr (L2_ONLY)
+        v[c] = __ldcg(src);  // rows written by other CTAs of the same kernel
+      else
+        v[c] = *src;
     }
     if constexpr (NORM) {
       double ss = 0.0;

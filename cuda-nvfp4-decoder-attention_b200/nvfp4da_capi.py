@@ -26,7 +26,11 @@ EXPORTED = (
     "nvfp4da_w4a16_linear", "nvfp4da_kv_cache_append", "nvfp4da_gqa_attention_workspace_size",
     "nvfp4da_gqa_attention_cached", "nvfp4da_forward_workspace_size", "nvfp4da_decoder_attention_forward",
     "nvfp4da_qkv_rope_append", "nvfp4da_decoder_attention_forward_noalloc",
+    "nvfp4da_decoder_attention_forward_path", "nvfp4da_forward_step_supported", "nvfp4da_forward_sync_status",
+    "nvfp4da_debug_wait_timeout",
 )
+
+PATH_AUTO, PATH_CHAIN, PATH_STEP = 0, 1, 2
 
 
 class CapiError(RuntimeError):
@@ -86,6 +90,10 @@ def load() -> C.CDLL:
         "nvfp4da_decoder_attention_forward": (C.c_int, [C.POINTER(ForwardArgs), vp, sz, vp]),
         "nvfp4da_qkv_rope_append": (C.c_int, [C.POINTER(ForwardArgs), vp, vp]),
         "nvfp4da_decoder_attention_forward_noalloc": (C.c_int, [C.POINTER(ForwardArgs), vp]),
+        "nvfp4da_decoder_attention_forward_path": (C.c_int, [C.POINTER(ForwardArgs), vp, sz, vp, C.c_int]),
+        "nvfp4da_forward_step_supported": (C.c_int, [C.POINTER(ForwardArgs)]),
+        "nvfp4da_forward_sync_status": (C.c_int, [vp, C.POINTER(C.c_uint), C.c_int]),
+        "nvfp4da_debug_wait_timeout": (C.c_int, [vp, C.c_ulonglong, C.POINTER(C.c_uint)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -190,10 +198,25 @@ def quantize(source: torch.Tensor, stream=None):
     return packed, scales, gamma
 
 
+def sync_status(stream=None, clear: bool = True) -> int:
+    """Error flags of one-kernel steps on ``stream`` (bit 0: a bounded wait
+    timed out); synchronises the stream."""
+    flags = C.c_uint(0)
+    _check(load().nvfp4da_forward_sync_status(_stream(stream), C.byref(flags), 1 if clear else 0))
+    return flags.value
+
+
+def wait_timeout_probe(timeout_ns: int, stream=None) -> int:
+    """Run the bounded-wait self-test; returns its error flags."""
+    flags = C.c_uint(0)
+    _check(load().nvfp4da_debug_wait_timeout(_stream(stream), timeout_ns, C.byref(flags)))
+    return flags.value
+
+
 class Forward:
     """A prepared forward call: arguments and workspace bound once, then
-    ``run()`` re-launches the three kernels (the form a serving loop or a CUDA
-    graph capture uses)."""
+    ``run()`` re-launches the kernels (the form a serving loop or a CUDA graph
+    capture uses)."""
 
     def __init__(self, x, input_norm_weight, q_w, k_w, v_w, q_norm_weight, k_norm_weight, o_w, k_cache, v_cache,
                  output, past_length: int = 0, past_lengths: torch.Tensor | None = None,
@@ -227,9 +250,15 @@ class Forward:
             raise CapiError(ERR_INVALID_ARGUMENT, lib.nvfp4da_last_error().decode())
         self.workspace = torch.empty(self.workspace_bytes, dtype=torch.uint8, device=x.device)
 
-    def run(self, stream=None) -> None:
-        _check(load().nvfp4da_decoder_attention_forward(C.byref(self.args), _p(self.workspace),
-                                                         self.workspace_bytes, _stream(stream)))
+    def run(self, stream=None, path: int = PATH_AUTO) -> None:
+        """One forward; ``path`` picks the kernels (PATH_AUTO: the one-kernel
+        decode step where it applies, else the three-kernel chain)."""
+        _check(load().nvfp4da_decoder_attention_forward_path(C.byref(self.args), _p(self.workspace),
+                                                              self.workspace_bytes, _stream(stream), path))
+
+    @property
+    def step_supported(self) -> bool:
+        return bool(load().nvfp4da_forward_step_supported(C.byref(self.args)))
 
     def run_qkv(self, q_rope_out: torch.Tensor, stream=None) -> None:
         """Only the fused front half (norm, QKV, per-head norm, RoPE, append)."""

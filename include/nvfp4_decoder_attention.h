@@ -152,6 +152,35 @@ size_t nvfp4da_forward_workspace_size(const nvfp4da_forward_args* args);
 int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* workspace, size_t workspace_bytes,
                                       void* stream);
 
+/* Forward with an explicit kernel path.  NVFP4DA_PATH_AUTO (what
+ * nvfp4da_decoder_attention_forward uses) takes the one-kernel decode step
+ * when it covers the call, else the three-kernel chain; NVFP4DA_PATH_CHAIN
+ * always takes the chain; NVFP4DA_PATH_STEP takes the one-kernel step or fails
+ * with NVFP4DA_ERR_UNSUPPORTED.  Same results within the numerics policy (the
+ * FP32 summation order of the projections and of the attention splits
+ * differs).  The one-kernel step covers T == 1, B <= 8, hidden % 256 == 0,
+ * hidden <= 4096, head_dim in {64, 128, 256}, 1/2/4/8 query heads per KV head,
+ * no stage outputs, and a K/V tile per split that fits in shared memory.  It
+ * is a cooperative launch whose phases are ordered by counters in a
+ * library-owned slot of the stream it is launched on (64 slots per device):
+ * a graph that captured it must not be replayed concurrently with other
+ * forwards issued to the capturing stream.  No counterpart in the reference
+ * (its forward is always the modular chain). */
+#define NVFP4DA_PATH_AUTO 0
+#define NVFP4DA_PATH_CHAIN 1
+#define NVFP4DA_PATH_STEP 2
+int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* args, void* workspace, size_t workspace_bytes,
+                                           void* stream, int path);
+/* 1 if the one-kernel decode step covers args, else 0. */
+int nvfp4da_forward_step_supported(const nvfp4da_forward_args* args);
+/* Error flags recorded by one-kernel steps on `stream` (bit 0: a bounded wait
+ * timed out); synchronises the stream; clears them if `clear`.  No
+ * counterpart in the reference. */
+int nvfp4da_forward_sync_status(void* stream, unsigned* flags, int clear);
+/* Self-test of the bounded wait used by the one-kernel step: one CTA waits on
+ * a counter that nothing sets, gives up after timeout_ns and reports the
+ * timeout in *flags (bit 0).  Synchronises the stream. */
+int nvfp4da_debug_wait_timeout(void* stream, unsigned long long timeout_ns, unsigned* flags);
 /* The fused front half of the forward on its own: input RMSNorm, Q/K/V
  * projection, per-head Q/K RMSNorm, RoPE and the K/V append, one kernel.
  * Replaces the reference's chain cuda_rms_norm -> 3x cuda_w4a16_linear ->

@@ -1,0 +1,206 @@
+"""GPU parity of the one-kernel decode step (NVFP4DA_PATH_STEP) through the C ABI.
+
+The step kernel computes the same forward as the three-kernel chain in one
+cooperative launch.  Per case:
+* the output against the oracle run end to end on the same inputs (scale-
+  relative policy) and against the chain path on the same inputs;
+* the cache: every slot but P_b unchanged bit for bit; the appended V row
+  within one BF16 step of the oracle's V projection, the appended K row within
+  the attention policy of the oracle's K after norm and RoPE;
+* no bounded wait gave up (the stream's sync status stays 0).
+Plus repeated launches, graph replay, two streams at once, and the bounded-
+wait self-test.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from bf16_metrics import assert_attention_policy, assert_e2e_policy, assert_stage_policy
+from gpu_util import dev_weight, host_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def make_case(b, h, hkv, d, pasts, c, seed):
+    import synthetic
+
+    pasts = tuple(pasts) if not np.isscalar(pasts) else (pasts,)
+    shape = synthetic.DecodeShape(batch=b, tokens=1, hidden=h, kv_heads=hkv, head_dim=d, capacity=c,
+                                  past_lengths=pasts)
+    inp = synthetic.make_decode_inputs(shape, seed)
+    host_w = {k: oracle.quantize(w.numpy()) for k, w in inp.weights_fp32.items()}
+    return inp, host_w
+
+
+def forward(inp, ws, pasts, kc, vc, path):
+    import nvfp4da_capi
+
+    out = torch.empty_like(inp.x, device="cuda")
+    pl = None
+    past, maxp = int(np.max(pasts)), int(np.max(pasts))
+    if not np.isscalar(pasts) and len(set(pasts)) > 1:
+        pl = torch.tensor(pasts, dtype=torch.int64).cuda()
+        past = 0
+    fw = nvfp4da_capi.Forward(inp.x.cuda(), inp.input_norm_weight.cuda(), ws["q"], ws["k"], ws["v"],
+                              inp.q_norm_weight.cuda(), inp.k_norm_weight.cuda(), ws["o"], kc, vc, out,
+                              past_length=past, past_lengths=pl, max_past_length=maxp)
+    return fw, out
+
+
+STEP_CASES = [
+    # b, h, hkv, d, past(s), c
+    (1, 3072, 6, 128, 511, 1024),          # configs[0]
+    (1, 3072, 6, 128, 0, 1024),            # empty cache: one split, RoPE at position 0
+    (1, 3072, 6, 128, 40, 64),             # one split, no partials
+    (1, 3072, 6, 128, 4000, 4096),         # the longest tile that fits in shared memory
+    (3, 256, 2, 64, 40, 64),               # D = 64, 2 query heads per KV head
+    (1, 512, 1, 256, 9, 16),               # D = 256
+    (8, 1024, 8, 128, 100, 128),           # 8 sequences, 1 query head per KV head
+    (2, 2048, 2, 128, 700, 1024),          # 8 query heads per KV head
+    (4, 3072, 6, 128, (5, 300, 511, 64), 512),  # per-sequence lengths (device array)
+    (2, 3072, 6, 128, (1023, 17), 1024),
+]
+
+
+@pytest.mark.parametrize("b,h,hkv,d,pasts,c", STEP_CASES)
+def test_step_matches_oracle_and_chain(b, h, hkv, d, pasts, c):
+    import nvfp4da_capi
+
+    inp, host_w = make_case(b, h, hkv, d, pasts, c, seed=b * 1000 + h + d)
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    pl = np.broadcast_to(np.asarray(pasts, dtype=np.int64), (b,))
+    kc_before = host_bits(inp.k_cache)
+    vc_before = host_bits(inp.v_cache)
+
+    kc, vc = inp.k_cache.cuda(), inp.v_cache.cuda()
+    fw, out = forward(inp, ws, pasts, kc, vc, nvfp4da_capi.PATH_STEP)
+    assert fw.step_supported
+    fw.run(path=nvfp4da_capi.PATH_STEP)
+    assert nvfp4da_capi.sync_status() == 0
+    out_bits, kc_bits, vc_bits = host_bits(out), host_bits(kc), host_bits(vc)
+
+    kc2, vc2 = inp.k_cache.cuda(), inp.v_cache.cuda()
+    fw2, out2 = forward(inp, ws, pasts, kc2, vc2, nvfp4da_capi.PATH_CHAIN)
+    fw2.run(path=nvfp4da_capi.PATH_CHAIN)
+    torch.cuda.synchronize()
+    chain_bits = host_bits(out2)
+
+    g_q, g_k = host_bits(inp.q_norm_weight), host_bits(inp.k_norm_weight)
+    ref = oracle.decoder_attention_nvfp4(host_bits(inp.x), host_bits(inp.input_norm_weight), host_w["q"],
+                                         host_w["k"], host_w["v"], g_q, g_k, host_w["o"], kc_before.copy(),
+                                         vc_before.copy(), pl if b > 1 else int(pl[0]))
+    assert_e2e_policy(out_bits, ref.output)
+    assert_e2e_policy(out_bits, chain_bits)
+
+    # Cache: only slot P_b of each sequence changes.
+    for i in range(b):
+        p = int(pl[i])
+        for after, before in ((kc_bits, kc_before), (vc_bits, vc_before)):
+            np.testing.assert_array_equal(after[i, :, :p], before[i, :, :p])
+            np.testing.assert_array_equal(after[i, :, p + 1:], before[i, :, p + 1:])
+        v_new = ref.v_projected[i].reshape(1, hkv, d).transpose(1, 0, 2)
+        assert_stage_policy(vc_bits[i, :, p:p + 1], v_new)
+        assert_attention_policy(kc_bits[i, :, p:p + 1], ref.k_rope[i].transpose(1, 0, 2))
+
+
+def test_step_is_deterministic_and_reusable_across_launches_and_graphs():
+    """Many launches on one stream reuse one synchronisation slot; a graph
+    replay reuses it too.  Every launch must give the same bits."""
+    import nvfp4da_capi
+
+    inp, host_w = make_case(1, 3072, 6, 128, 511, 1024, seed=3)
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    kc, vc = inp.k_cache.cuda(), inp.v_cache.cuda()
+    fw, out = forward(inp, ws, 511, kc, vc, nvfp4da_capi.PATH_STEP)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        fw.run(s)
+        first = out.clone()
+        for _ in range(50):
+            fw.run(s)
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), first.view(torch.int16))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(4):
+                fw.run(s)
+        out.zero_()
+        for _ in range(10):
+            g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), first.view(torch.int16))
+    assert nvfp4da_capi.sync_status(s) == 0
+
+
+def test_step_on_two_streams_at_once():
+    """Launches on different streams take different slots and may overlap."""
+    import nvfp4da_capi
+
+    inp, host_w = make_case(1, 3072, 6, 128, 511, 1024, seed=4)
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    runs = []
+    for _ in range(2):
+        kc, vc = inp.k_cache.cuda(), inp.v_cache.cuda()
+        runs.append(forward(inp, ws, 511, kc, vc, nvfp4da_capi.PATH_STEP))
+    ref_fw, ref_out = runs[0]
+    ref_fw.run()
+    torch.cuda.synchronize()
+    expected = ref_out.clone()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for _ in range(20):
+        for (fw, _), st in zip(runs, streams):
+            fw.run(st)
+    torch.cuda.synchronize()
+    for (_, out), st in zip(runs, streams):
+        assert torch.equal(out.view(torch.int16), expected.view(torch.int16))
+        assert nvfp4da_capi.sync_status(st) == 0
+
+
+def test_auto_path_takes_the_step_kernel_where_it_applies():
+    import nvfp4da_capi
+
+    inp, host_w = make_case(1, 3072, 6, 128, 511, 1024, seed=5)
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    fw, out = forward(inp, ws, 511, inp.k_cache.cuda(), inp.v_cache.cuda(), nvfp4da_capi.PATH_AUTO)
+    fw.run()
+    auto = out.clone()
+    fw2, out2 = forward(inp, ws, 511, inp.k_cache.cuda(), inp.v_cache.cuda(), nvfp4da_capi.PATH_STEP)
+    fw2.run(path=nvfp4da_capi.PATH_STEP)
+    torch.cuda.synchronize()
+    assert torch.equal(auto.view(torch.int16), out2.view(torch.int16))
+
+
+@pytest.mark.parametrize("b,h,hkv,d,pasts,c", [
+    (1, 96, 1, 48, 5, 9),                          # D = 48
+    (4, 3072, 6, 128, (5, 300, 1023, 64), 1024),   # K/V tiles too large for shared memory
+])
+def test_step_path_rejects_what_it_does_not_cover(b, h, hkv, d, pasts, c):
+    """Configurations the one-kernel step does not cover: PATH_STEP refuses
+    them, PATH_AUTO falls back to the chain."""
+    import nvfp4da_capi
+
+    inp, host_w = make_case(b, h, hkv, d, pasts, c, seed=6)
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    fw, out = forward(inp, ws, pasts, inp.k_cache.cuda(), inp.v_cache.cuda(), nvfp4da_capi.PATH_STEP)
+    assert not fw.step_supported
+    with pytest.raises(nvfp4da_capi.CapiError) as e:
+        fw.run(path=nvfp4da_capi.PATH_STEP)
+    assert e.value.status == nvfp4da_capi.ERR_UNSUPPORTED
+    fw.run()
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+
+
+def test_bounded_wait_gives_up_and_reports():
+    """The wait primitive of the step kernel, on a counter nothing sets: it
+    must return after its time limit with the timeout flag set, and the
+    context must stay usable."""
+    import nvfp4da_capi
+
+    assert nvfp4da_capi.wait_timeout_probe(2_000_000) == 1  # 2 ms limit
+    x = torch.ones(4, device="cuda")
+    assert float((x + 1).sum()) == 8.0
