@@ -285,6 +285,10 @@ def run_gpu(args) -> None:
                                                               r.out.view(1, 3072), stream)) for r in reps],
                               reps_k, stream),
     }
+    # both forward paths, whole steps (the same graph form as the timed region)
+    path_ms = {name: timed_graph([(lambda r=r, pth=pth: r.fw.run(stream, pth)) for r in reps], reps_k, stream)
+               for name, pth in (("chain", capi.PATH_CHAIN), ("step", capi.PATH_STEP))
+               if pth != capi.PATH_STEP or reps[0].fw.step_supported}
     per_launch_us = {n: v * 1e3 / (reps_k * n_rep) for n, v in kern_ms.items()}
     peak, peak_src = measured_peak_gbs()
     kernels = {n: {"us": round(per_launch_us[n], 3), "bytes": nbytes[n],
@@ -316,6 +320,7 @@ def run_gpu(args) -> None:
                      "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
                      "step_bytes": nbytes["step"]},
         "kernels": kernels,
+        "paths_us_per_step": {n: round(v * 1e3 / (reps_k * n_rep), 3) for n, v in path_ms.items()},
         "e2e": e2e,
         "gpu_launches": 3 * k,
         "clocks": clk,

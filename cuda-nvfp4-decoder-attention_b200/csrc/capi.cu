@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <map>
@@ -641,11 +642,12 @@ const void* step_kernel_ptr(int epl, int gh) {
 
 struct StepPlan {
   int epl, gh;
-  int rq, n_qkv, ro, ro_rows, n_o;
-  int splits, split_len, grid;
+  int rq, n_qkv;
+  int o_rows_big, o_n_big, o_rows_small, o_tile_rows;
+  int splits, split_len, grid, o_combine;
   uint32_t smem;
-  uint32_t off_qs, off_qw, off_os, off_ow, off_kv, off_q, off_xs, off_x16, off_red;
-  size_t proj, ctx, partials, total;  // workspace offsets / bytes
+  uint32_t off_qs, off_qw, off_kv, off_q, off_comb, off_os, off_ow, off_xs, off_x16, off_red;
+  size_t proj, ctx, part_o, part_ml, total;  // workspace offsets / bytes
 };
 
 // Static shared memory of a step-kernel instantiation (cached per device).
@@ -696,9 +698,12 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
     }
   }
   if (!rq) return false;
-  const int ro = static_cast<int>(ceil_div(k, grid));
+  // O rows in units of 8, spread over every CTA: o_n_big CTAs take one unit more.
+  const int64_t units8 = k / 8;
+  const int64_t per = units8 / grid, n_big = units8 - per * grid;
+  const int rows_big = static_cast<int>(8 * (per + (n_big > 0 ? 1 : 0)));
   int tiles = 1;
-  while (16 * tiles < ro) tiles <<= 1;
+  while (16 * tiles < rows_big) tiles <<= 1;
   if (16 * tiles > kStepMaxRows) return false;
   const int64_t bh = nb * hkv;
   if (bh > grid) return false;
@@ -710,9 +715,10 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   s.gh = static_cast<int>(group);
   s.rq = rq;
   s.n_qkv = static_cast<int>(nqkv / rq);
-  s.ro = ro;
-  s.ro_rows = 16 * tiles;
-  s.n_o = static_cast<int>(ceil_div(k, ro));
+  s.o_rows_big = rows_big;
+  s.o_n_big = static_cast<int>(n_big > 0 ? n_big : grid);
+  s.o_rows_small = static_cast<int>(8 * per);
+  s.o_tile_rows = 16 * tiles;
   s.splits = static_cast<int>(splits);
   s.split_len = static_cast<int>(split_len);
   s.grid = grid;
@@ -723,30 +729,51 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
     return static_cast<uint32_t>(o);
   };
   const uint64_t ks = k / 16, kb = k / 2;
+  // Overlay region: QKV rows, K/V tile (later the warps' o vectors and split
+  // weights) and q; after the attention unit, the split partials.
+  const uint64_t tile = 2ull * split_len * d * 2, smo = 1ull * kStepWarps * group * d * 4,
+                 comb_w = 1ull * group * splits * 4;
   s.off_qs = take(rq * ks);
   s.off_qw = take(rq * kb);
-  // Only the RO rows a CTA owns are stored; the MMA tiles read up to ro_rows
-  // rows, the rows past RO landing in the buffers that follow (in bounds,
-  // their outputs are discarded).
-  s.off_os = take(ro * ks);
-  s.off_ow = take(ro * kb);
-  const uint64_t tile = 2ull * split_len * d * 2, smo = 1ull * kStepWarps * group * d * 4,
-                 comb = 2ull * group * splits * 4;
-  s.off_kv = take(std::max(tile, std::max(smo, comb)));
+  s.off_kv = take(std::max(tile, std::max(smo, comb_w)));
   s.off_q = take(group * d * 4);
+  const uint64_t front = off;
+  const uint64_t items = nb * hq;
+  const uint64_t comb = items * splits * d * 4 + items * splits * 16;
+  // The O CTAs combine the partials themselves when they fit beside the rest.
+  s.o_combine = 0;
+  off = std::max(front, comb);
+  s.off_comb = 0;
+  const uint64_t rest = (rows_big * ks + 127) / 128 * 128 + (rows_big * kb + 127) / 128 * 128 +
+                        2 * ((nb * k * 2 + 127) / 128 * 128) + kMmaWarps * 128 * 4;
+  // Measured on B200: all 148 CTAs bulk-reading the same partials is slower
+  // than the last-arriver combine, so the combine-in-O variant stays off by
+  // default (kept for configurations with few, small partials).
+  constexpr bool kPreferOCombine = false;
+  if (kPreferOCombine && off + rest + static_smem(fn) <= kMaxDynSmem) {
+    s.o_combine = 1;
+  } else {
+    off = front;
+  }
+  s.off_os = take(rows_big * ks);
+  s.off_ow = take(rows_big * kb);
   s.off_xs = take(nb * k * 2);
   s.off_x16 = take(nb * k * 2);
   s.off_red = take(kMmaWarps * 128 * 4);
   if (off + static_smem(fn) > kMaxDynSmem) return false;
-  if (s.off_ow + static_cast<uint64_t>(s.ro_rows) * kb > off) return false;
+  // The MMA tiles read up to o_tile_rows rows; the rows past the CTA's own
+  // land in the buffers that follow (in bounds, their outputs discarded).
+  if (s.off_ow + static_cast<uint64_t>(s.o_tile_rows) * kb > off) return false;
   s.smem = static_cast<uint32_t>(off);
   size_t w = 0;
   s.proj = w;
   w += align_up(static_cast<size_t>(nb * nqkv) * 2, 256);
   s.ctx = w;
   w += align_up(static_cast<size_t>(nb * k) * 2, 256);
-  s.partials = w;
-  if (splits > 1) w += align_up(static_cast<size_t>(nb * hq) * splits * (d + 2) * 4, 256);
+  s.part_o = w;
+  w += align_up(static_cast<size_t>(items) * splits * d * 4, 256);
+  s.part_ml = w;
+  w += align_up(static_cast<size_t>(items) * splits * 16, 256);
   s.total = w;
   return true;
 }
@@ -780,25 +807,33 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   p.theta = a->rope_theta;
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(a->head_dim)));
   p.rq = pl.rq;
-  p.rq_rows = pl.rq;
   p.n_qkv_blocks = pl.n_qkv;
-  p.ro = pl.ro;
-  p.ro_rows = pl.ro_rows;
-  p.n_o_blocks = pl.n_o;
+  p.o_rows_big = pl.o_rows_big;
+  p.o_n_big = pl.o_n_big;
+  p.o_rows_small = pl.o_rows_small;
+  p.o_tile_rows = pl.o_tile_rows;
   p.splits = pl.splits;
   p.split_len = pl.split_len;
+  p.o_combine = pl.o_combine;
   char* base = static_cast<char*>(ws);
   p.proj = reinterpret_cast<uint16_t*>(base + pl.proj);
   p.ctx = reinterpret_cast<uint16_t*>(base + pl.ctx);
-  p.partials = reinterpret_cast<float*>(base + pl.partials);
+  p.part_o = reinterpret_cast<float*>(base + pl.part_o);
+  p.part_ml = reinterpret_cast<float*>(base + pl.part_ml);
   p.sync = slot;
   p.timeout_ns = 500ull * 1000 * 1000;
+  p.sched = 1;
+#ifdef NVFP4DA_PHASES
+  if (const char* v = std::getenv("NVFP4DA_STEP_SCHED")) p.sched = std::atoi(v);
+  if (const char* v = std::getenv("NVFP4DA_STEP_OCOMB")) p.o_combine = p.o_combine && std::atoi(v);
+#endif
   p.off_qs = pl.off_qs;
   p.off_qw = pl.off_qw;
-  p.off_os = pl.off_os;
-  p.off_ow = pl.off_ow;
   p.off_kv = pl.off_kv;
   p.off_q = pl.off_q;
+  p.off_comb = pl.off_comb;
+  p.off_os = pl.off_os;
+  p.off_ow = pl.off_ow;
   p.off_xs = pl.off_xs;
   p.off_x16 = pl.off_x16;
   p.off_red = pl.off_red;
@@ -1003,8 +1038,12 @@ int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* 
     return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "unknown forward path %d", path);
   ForwardLayout L;
   if ((r = plan_forward(a, L))) return r;
+  // AUTO takes the chain: on B200 the canonical decode step measures 23.0 us
+  // through the chain and 23.6 us through the one-kernel step.
+  constexpr bool kAutoPrefersStep = false;
   StepPlan sp;
-  const bool step_ok = path != NVFP4DA_PATH_CHAIN && plan_step(a, sp);
+  const bool step_ok = (path == NVFP4DA_PATH_STEP || (path == NVFP4DA_PATH_AUTO && kAutoPrefersStep)) &&
+                       plan_step(a, sp);
   if (path == NVFP4DA_PATH_STEP && !step_ok)
     return fail(NVFP4DA_ERR_UNSUPPORTED, "the one-kernel decode step does not cover this configuration");
   const size_t need = step_ok ? std::max(L.total, sp.total) : L.total;

@@ -25,9 +25,13 @@
 //    sequence b.  Waits for the counters of its GH query heads and its K and V
 //    head, applies the per-head RMSNorm + RoPE to those rows itself, appends
 //    the new K/V row to the cache (the split holding position P_b), runs the
-//    online-softmax loop over its K/V tile, and leaves (m, l, o) partials; the
-//    last split to arrive combines them into the BF16 context.
-//  * O block c: rows [c*RO, c*RO + RO) of Wo, after every context row is done.
+//    online-softmax loop over its K/V tile, and leaves (m, l, o) partials.
+//  * O block c: 8-row multiples of Wo (the rows spread over all CTAs).  When
+//    every split's partials fit in shared memory (o_combine) each O CTA
+//    bulk-copies all of them once every unit has signalled and does the
+//    log-sum-exp combine itself -- no extra hand-off; otherwise the last split
+//    of each (b, kv head) to arrive combines them into a BF16 context buffer
+//    that the O CTAs read.
 //
 // Synchronisation state lives in a slot of library-owned device memory (one
 // slot per stream), zero between launches: the last CTA to leave clears it.
@@ -66,17 +70,23 @@ struct StepParams {
   const int64_t* past_lengths;
   float eps, theta, scale;
   // plan
-  int rq, rq_rows, n_qkv_blocks;  // rows per QKV block, tile-padded rows
-  int ro, ro_rows, n_o_blocks;
+  int rq, n_qkv_blocks;                        // QKV rows per block (divides D)
+  int o_rows_big, o_n_big, o_rows_small, o_tile_rows;  // O rows per CTA: big for CTAs < o_n_big
   int splits, split_len;
+  int o_combine;  // 1: O CTAs combine the split partials themselves
   // workspace
-  uint16_t* proj;   // [B, (Hq + 2 Hkv) D] raw projections
-  uint16_t* ctx;    // [B, H]
-  float* partials;  // [B * Hq, splits, D + 2]
-  unsigned* sync;   // slot
+  uint16_t* proj;    // [B, (Hq + 2 Hkv) D] raw projections
+  uint16_t* ctx;     // [B, H]            (o_combine == 0)
+  float* part_o;     // [B * Hq, splits, D]
+  float* part_ml;    // [B * Hq, splits, 4]  (m, l, -, -)
+  unsigned* sync;    // slot
   unsigned long long timeout_ns;
-  // dynamic shared-memory layout (byte offsets)
-  uint32_t off_qs, off_qw, off_os, off_ow, off_kv, off_q, off_xs, off_x16, off_red;
+  // When the K/V tile and the O rows are requested: 0 at launch, 1 once the
+  // QKV rows have landed, 2 the K/V tile then and the O rows after the
+  // attention unit.
+  int sched;
+  // dynamic shared-memory layout (byte offsets); qs/qw/kv/q and comb overlay
+  uint32_t off_qs, off_qw, off_kv, off_q, off_comb, off_os, off_ow, off_xs, off_x16, off_red;
   // cos/sin of RoPE at position past_length (rope_host_ok), else computed on the device
   int rope_host_ok;
   float2 rope_host[kMaxHeadDim / 2];
@@ -96,12 +106,19 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 // Publish this CTA's global writes, then add 1 to *ctr.  All threads call.
+// The barrier orders every thread's writes before thread 0's release, and a
+// release is cumulative over what its thread has observed.
 __device__ __forceinline__ void cta_signal(unsigned* ctr) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
-  }
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
+// Returns the counter's previous value (acquire + release: the caller sees
+// the writes of every CTA that added before it).
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* ctr, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(ctr), "r"(v) : "memory");
+  return old;
 }
 
 // Wait (all threads call; warp 0 polls) until ctr[idx[i]] >= target for the n
@@ -121,7 +138,6 @@ __device__ __forceinline__ void cta_wait(const unsigned* ctr, const int* idx, in
         break;
       }
     }
-    __threadfence();
   }
   __syncthreads();
 }
@@ -130,15 +146,26 @@ __device__ __forceinline__ void cta_wait(const unsigned* ctr, const int* idx, in
 template <int EPL, int GH>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t bar_qkv, bar_kv, bar_o;
+  __shared__ uint64_t bar_qkv, bar_kv, bar_o, bar_c;
   __shared__ float redf[2 * kStepWarps];
   __shared__ double redd[2 * kStepWarps];
   __shared__ float escale[kMmaMaxM];
+  __shared__ float red_small[kMmaMaxM * kStepWarps];
   __shared__ float outv[kStepMaxRows * 8];
   __shared__ float sm_m[kStepWarps][GH], sm_l[kStepWarps][GH], wf[kStepWarps][GH], cta_m[GH], cta_l[GH];
   __shared__ unsigned s_flag;
   [[maybe_unused]] constexpr unsigned kPhaseBase = 3072;
+  constexpr int PPL = EPL / 2;  // RoPE pairs per lane (D = 32 * EPL)
   NVFP4DA_PHASE(0);
+#ifdef NVFP4DA_PHASES
+  if (p.sched & 32) {  // diagnostic: touch every line of the parameter block at once
+    constexpr int kLines = (sizeof(StepParams) + 127) / 128;
+    if (threadIdx.x < kLines) {
+      const uint32_t v = reinterpret_cast<const uint32_t*>(&p)[threadIdx.x * 32];
+      asm volatile("" ::"r"(v));
+    }
+  }
+#endif
 
   const int cta = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -146,10 +173,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   const int mrows = static_cast<int>(nb);  // T = 1: one activation row per sequence
   const int64_t hq = p.q_heads, hkv = p.kv_heads;
   const int64_t nqkv = (hq + 2 * hkv) * d;
+  const int ns = p.splits;
   unsigned* sync = p.sync;
   unsigned* err = sync + kSyncErr;
-  unsigned* head_done = sync + kSyncHeads;                 // [Hq + 2 Hkv]
-  unsigned* arrive = head_done + (hq + 2 * hkv);           // [B * Hkv]
+  unsigned* head_done = sync + kSyncHeads;        // [Hq + 2 Hkv]
+  unsigned* arrive = head_done + (hq + 2 * hkv);  // [B * Hkv]
 
   uint8_t* qs_smem = smem + p.off_qs;
   uint8_t* qw_smem = smem + p.off_qw;
@@ -164,18 +192,26 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   // ---- roles
   const bool has_qkv = cta < p.n_qkv_blocks;
-  const bool has_o = cta < p.n_o_blocks;
-  const int n_units = static_cast<int>(nb * hkv) * p.splits;
+  const int n_units = static_cast<int>(nb * hkv) * ns;
   const bool has_attn = cta < n_units;
+  int64_t orow0;
+  int o_rows;
+  if (cta < p.o_n_big) {
+    o_rows = p.o_rows_big;
+    orow0 = static_cast<int64_t>(cta) * p.o_rows_big;
+  } else {
+    o_rows = p.o_rows_small;
+    orow0 = static_cast<int64_t>(p.o_n_big) * p.o_rows_big + static_cast<int64_t>(cta - p.o_n_big) * p.o_rows_small;
+  }
+  const int o_valid = orow0 < k ? static_cast<int>((k - orow0) < o_rows ? (k - orow0) : o_rows) : 0;
+  const bool has_o = o_valid > 0;
 
   const int64_t qrow0 = static_cast<int64_t>(cta) * p.rq;  // concatenated QKV row
   const int mat = qrow0 < hq * d ? 0 : (qrow0 < (hq + hkv) * d ? 1 : 2);
   const int64_t mat_row0 = qrow0 - (mat == 0 ? 0 : (mat == 1 ? hq * d : (hq + hkv) * d));
-  const int64_t orow0 = static_cast<int64_t>(cta) * p.ro;
-  const int o_valid = has_o ? static_cast<int>((k - orow0) < p.ro ? (k - orow0) : p.ro) : 0;
 
-  const int split = has_attn ? cta % p.splits : 0;
-  const int64_t bh = has_attn ? cta / p.splits : 0;
+  const int split = has_attn ? cta % ns : 0;
+  const int64_t bh = has_attn ? cta / ns : 0;
   const int64_t b = bh / hkv, kvh = bh % hkv;
   const int64_t pb = has_attn ? (p.past_lengths ? p.past_lengths[b] : p.past_length) : 0;
   const int64_t s0 = static_cast<int64_t>(split) * p.split_len;
@@ -183,62 +219,92 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   // length says.
   int64_t s_end = pb + 1 < p.capacity ? pb + 1 : p.capacity;
   if (s_end > s0 + p.split_len) s_end = s0 + p.split_len;
-  int64_t cache_end = pb < s_end ? pb : s_end;  // rows [s0, cache_end) come from the cache
+  const int64_t cache_end = pb < s_end ? pb : s_end;  // rows [s0, cache_end) come from the cache
   const int64_t n_cache = cache_end > s0 ? cache_end - s0 : 0;
   const bool owns_new = has_attn && pb >= 0 && pb < p.capacity && pb >= s0 && pb < s0 + p.split_len;
   const uint16_t* kbase = p.k_cache + (b * hkv + kvh) * p.capacity * d;
   const uint16_t* vbase = p.v_cache + (b * hkv + kvh) * p.capacity * d;
 
-  if (threadIdx.x == 0) {
-    mbar_init(&bar_qkv, 1);
-    mbar_init(&bar_kv, 1);
-    mbar_init(&bar_o, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  // ---- put every input slice of this CTA in flight (none is written by the step)
-  if (threadIdx.x == 0) {
-    const int64_t ks = k / 16, kb = k / 2;
-    if (has_qkv) {
-      const uint32_t sb = static_cast<uint32_t>(p.rq * ks), wb = static_cast<uint32_t>(p.rq * kb);
-      mbar_arrive_expect_tx(&bar_qkv, sb + wb);
-      bulk_g2s(qs_smem, p.scales[mat] + mat_row0 * ks, sb, &bar_qkv);
-      bulk_g2s(qw_smem, p.packed[mat] + mat_row0 * kb, wb, &bar_qkv);
-    }
-    if (n_cache > 0) {
-      const uint32_t tb = static_cast<uint32_t>(n_cache * d * 2);
-      mbar_arrive_expect_tx(&bar_kv, 2 * tb);
-      bulk_g2s(kv_k, kbase + s0 * d, tb, &bar_kv);
-      bulk_g2s(kv_v, vbase + s0 * d, tb, &bar_kv);
-    }
-    if (has_o) {
-      const uint32_t sb = static_cast<uint32_t>(o_valid * ks), wb = static_cast<uint32_t>(o_valid * kb);
-      mbar_arrive_expect_tx(&bar_o, sb + wb);
-      bulk_g2s(os_smem, p.scales[3] + orow0 * ks, sb, &bar_o);
-      bulk_g2s(ow_smem, p.packed[3] + orow0 * kb, wb, &bar_o);
-    }
-  }
-  NVFP4DA_PHASE(1);
-
-  // ---- input RMSNorm of the activation rows -> MMA operand (every CTA)
+  // ---- the activation rows and the input-norm gain first: they head the
+  // critical path, so their requests go out before any bulk traffic.
   constexpr int NCH = 2;
   uint4 gch[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int idx = threadIdx.x + c * kStepThreads;
     gch[c] = idx < k / 8 ? ldg_stream(p.g_in + 8 * idx) : make_uint4(0u, 0u, 0u, 0u);
+    if (idx < k / 8)
+      for (int m = 0; m < mrows; ++m) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + m * k + 8 * idx));
   }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_qkv, 1);
+    mbar_init(&bar_kv, 1);
+    mbar_init(&bar_o, 1);
+    mbar_init(&bar_c, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ---- input slices of this CTA (none is written by the step): the QKV
+  // rows now, the K/V tile and the O rows later (p.sched), so that they do
+  // not queue ahead of the critical path.
+  const int64_t ks = k / 16, kb = k / 2;
+  auto issue_kv = [&]() {
+    if (n_cache > 0) {
+      const uint32_t tb = static_cast<uint32_t>(n_cache * d * 2);
+      mbar_arrive_expect_tx(&bar_kv, 2 * tb);
+      bulk_g2s(kv_k, kbase + s0 * d, tb, &bar_kv);
+      bulk_g2s(kv_v, vbase + s0 * d, tb, &bar_kv);
+    }
+  };
+  auto issue_o = [&]() {
+    if (has_o) {
+      const uint32_t sb = static_cast<uint32_t>(o_valid * ks), wb = static_cast<uint32_t>(o_valid * kb);
+      mbar_arrive_expect_tx(&bar_o, sb + wb);
+      bulk_g2s(os_smem, p.scales[3] + orow0 * ks, sb, &bar_o);
+      bulk_g2s(ow_smem, p.packed[3] + orow0 * kb, wb, &bar_o);
+    }
+  };
+  if (threadIdx.x == 0) {
+    if (has_qkv) {
+      const uint32_t sb = static_cast<uint32_t>(p.rq * ks), wb = static_cast<uint32_t>(p.rq * kb);
+      mbar_arrive_expect_tx(&bar_qkv, sb + wb);
+      bulk_g2s(qs_smem, p.scales[mat] + mat_row0 * ks, sb, &bar_qkv);
+      bulk_g2s(qw_smem, p.packed[mat] + mat_row0 * kb, wb, &bar_qkv);
+    }
+    if ((p.sched & 7) == 0 || !has_qkv) {
+      issue_kv();
+      issue_o();
+    }
+  }
+  NVFP4DA_PHASE(1);
+
+  // ---- input RMSNorm of the activation rows -> MMA operand, QKV GEMV
   if (has_qkv) {
     bool f16 = prep_rows_regs<NCH, true>(p.x, k, mrows, gch, p.eps, x_stage, x16, escale, redf, redd, nullptr);
     NVFP4DA_PHASE(2);
     mbar_wait_bounded(&bar_qkv, 0, err);
+    if (threadIdx.x == 0 && (p.sched & 7) != 0) {
+      issue_kv();
+      if ((p.sched & 7) == 1 || !has_attn) issue_o();
+    }
     NVFP4DA_PHASE(3);
+#ifdef NVFP4DA_PHASES
+    if (p.sched & 16) {  // diagnostic: one step per loop iteration (small loop body)
+      if (f16)
+        mma_gemv_pass_smem<true, 1>(qw_smem, qs_smem, reinterpret_cast<const uint16_t*>(x16), k, p.rq, p.rq, mrows,
+                                    mred, outv);
+      else
+        mma_gemv_pass_smem<false, 1>(qw_smem, qs_smem, x_stage, k, p.rq, p.rq, mrows, mred, outv);
+    } else
+#endif
     if (f16)
-      mma_gemv_pass_smem<true, 4>(qw_smem, qs_smem, reinterpret_cast<const uint16_t*>(x16), k, p.rq_rows, mrows,
+      mma_gemv_pass_smem<true, 4>(qw_smem, qs_smem, reinterpret_cast<const uint16_t*>(x16), k, p.rq, p.rq, mrows,
                                   mred, outv);
     else
-      mma_gemv_pass_smem<false, 4>(qw_smem, qs_smem, x_stage, k, p.rq_rows, mrows, mred, outv);
+      mma_gemv_pass_smem<false, 4>(qw_smem, qs_smem, x_stage, k, p.rq, p.rq, mrows, mred, outv);
+    NVFP4DA_PHASE(13);
     const float gamma = *p.gamma[mat];
     for (int i = threadIdx.x; i < p.rq * mrows; i += kStepThreads) {
       const int n = i / p.rq, r = i % p.rq;
@@ -262,37 +328,46 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     NVFP4DA_PHASE(5);
     // Per-head RMSNorm + RoPE of this unit's query heads (and, for the split
     // holding position P_b, of the new key; the new value is the raw
-    // projection) -- the arithmetic of the fused QKV epilogue.
+    // projection) -- the arithmetic of the fused QKV epilogue.  Lane l owns
+    // element pairs l, l + 32, ...: one read of the projection row.
     const int64_t nslot = pb - s0;
     for (int item = warp; item < GH + 2; item += kStepWarps) {
       const bool is_q = item < GH;
       if (!is_q && !owns_new) continue;
       const int64_t col = is_q ? (kvh * GH + item) * d : (item == GH ? (hq + kvh) * d : (hq + hkv + kvh) * d);
-      const uint16_t* y = p.proj + b * nqkv + col;
+      const uint32_t* y2 = reinterpret_cast<const uint32_t*>(p.proj + b * nqkv + col);
+      uint32_t pr2[PPL];
+#pragma unroll
+      for (int j = 0; j < PPL; ++j) pr2[j] = __ldcg(y2 + lane + 32 * j);
       if (item == GH + 1) {
-        uint16_t* dst = p.v_cache + ((b * hkv + kvh) * p.capacity + pb) * d;
-        for (int64_t e = lane; e < d; e += 32) {
-          const uint16_t v = __ldcg(y + e);
-          kv_v[nslot * d + e] = v;
-          dst[e] = v;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(p.v_cache + ((b * hkv + kvh) * p.capacity + pb) * d);
+        uint32_t* tile = reinterpret_cast<uint32_t*>(kv_v + nslot * d);
+#pragma unroll
+        for (int j = 0; j < PPL; ++j) {
+          tile[lane + 32 * j] = pr2[j];
+          dst[lane + 32 * j] = pr2[j];
         }
         continue;
       }
       double ss = 0.0;
-      for (int64_t e = lane; e < d; e += 32) {
-        const float v = bf16_bits_to_f32(__ldcg(y + e));
-        ss += static_cast<double>(v * v);
+#pragma unroll
+      for (int j = 0; j < PPL; ++j) {
+        const float a = __uint_as_float(pr2[j] << 16), c = __uint_as_float(pr2[j] & 0xffff0000u);
+        ss += static_cast<double>(a * a) + static_cast<double>(c * c);
       }
       ss = warp_sum_f64(ss);
       const float inv = rms_inverse(static_cast<float>(ss), static_cast<float>(d), p.eps);
-      const uint16_t* g = is_q ? p.g_q : p.g_k;
-      uint16_t* kdst = is_q ? nullptr : p.k_cache + ((b * hkv + kvh) * p.capacity + pb) * d;
-      for (int64_t pr = lane; pr < d / 2; pr += 32) {
-        const int64_t e = 2 * pr;
-        const uint16_t n0 =
-            f32_to_bf16_bits(__fmul_rn(__fmul_rn(bf16_bits_to_f32(__ldcg(y + e)), inv), bf16_bits_to_f32(g[e])));
+      const uint32_t* g2 = reinterpret_cast<const uint32_t*>(is_q ? p.g_q : p.g_k);
+      uint32_t* kdst =
+          is_q ? nullptr : reinterpret_cast<uint32_t*>(p.k_cache + ((b * hkv + kvh) * p.capacity + pb) * d);
+#pragma unroll
+      for (int j = 0; j < PPL; ++j) {
+        const int pr = lane + 32 * j;
+        const uint32_t gg = g2[pr];
+        const uint16_t n0 = f32_to_bf16_bits(
+            __fmul_rn(__fmul_rn(__uint_as_float(pr2[j] << 16), inv), __uint_as_float(gg << 16)));
         const uint16_t n1 = f32_to_bf16_bits(
-            __fmul_rn(__fmul_rn(bf16_bits_to_f32(__ldcg(y + e + 1)), inv), bf16_bits_to_f32(g[e + 1])));
+            __fmul_rn(__fmul_rn(__uint_as_float(pr2[j] & 0xffff0000u), inv), __uint_as_float(gg & 0xffff0000u)));
         uint16_t r0 = n0, r1 = n1;
         if (pb != 0) {
           float c, sn;
@@ -305,13 +380,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
           rope_pair(bf16_bits_to_f32(n0), bf16_bits_to_f32(n1), c, sn, r0, r1);
         }
         if (is_q) {
-          qf[item * d + e] = bf16_bits_to_f32(r0);
-          qf[item * d + e + 1] = bf16_bits_to_f32(r1);
+          qf[item * d + 2 * pr] = bf16_bits_to_f32(r0);
+          qf[item * d + 2 * pr + 1] = bf16_bits_to_f32(r1);
         } else {
-          kv_k[nslot * d + e] = r0;
-          kv_k[nslot * d + e + 1] = r1;
-          kdst[e] = r0;
-          kdst[e + 1] = r1;
+          const uint32_t both = static_cast<uint32_t>(r0) | (static_cast<uint32_t>(r1) << 16);
+          reinterpret_cast<uint32_t*>(kv_k + nslot * d)[pr] = both;
+          kdst[pr] = both;
         }
       }
     }
@@ -396,9 +470,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
     NVFP4DA_PHASE(7);
 
-    // ---- combine the eight warps (their o vectors reuse the K/V tile)
+    // ---- combine the eight warps (their o vectors reuse the K/V tile) and
+    // leave this split's (m, l, o) in the workspace
     __syncthreads();  // every warp is done with the tile
-    float* sm_o = reinterpret_cast<float*>(smem + p.off_kv);  // [warps][GH][32 * EPL]
+    float* sm_o = reinterpret_cast<float*>(smem + p.off_kv);  // [warps][GH][D]
     if (lane == 0) {
 #pragma unroll
       for (int g = 0; g < GH; ++g) {
@@ -425,61 +500,43 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       }
       cta_m[g] = mx;
       cta_l[g] = l;
+      float* ml = p.part_ml + ((b * hq + kvh * GH + g) * ns + split) * 4;
+      ml[0] = mx;
+      ml[1] = l;
     }
     __syncthreads();
-    const int ns = p.splits;
     for (int idx = threadIdx.x; idx < GH * d; idx += kStepThreads) {
       const int g = static_cast<int>(idx / d);
       const int64_t e = idx % d;
       float o = 0.0f;
 #pragma unroll
       for (int w = 0; w < kStepWarps; ++w) o = fmaf(sm_o[(w * GH + g) * 32 * EPL + e], wf[w][g], o);
-      const int64_t row = b * hq + kvh * GH + g;
-      if (ns == 1) {
-        p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, cta_l[g]));
-      } else {
-        float* dst = p.partials + (row * ns + split) * (d + 2);
-        dst[e] = o;
-        if (e == 0) {
-          dst[d] = cta_m[g];
-          dst[d + 1] = cta_l[g];
-        }
-      }
+      p.part_o[((b * hq + kvh * GH + g) * ns + split) * d + e] = o;
     }
-    bool combine = ns == 1;
-    if (ns > 1) {
+    if (p.o_combine) {
+      cta_signal(&sync[kSyncCtxDone]);  // counts units
+    } else {
       // The last split of (b, kv head) to arrive combines all of them.
       __syncthreads();
       if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&arrive[bh], 1u);
+        const unsigned prev = atom_add_acq_rel(&arrive[bh], 1u);
         s_flag = prev == static_cast<unsigned>(ns - 1) ? 1u : 0u;
-        __threadfence();
       }
       __syncthreads();
-      combine = s_flag != 0;
-      if (combine) {
+      if (s_flag) {
         NVFP4DA_PHASE(8);
-        // (m, l) of every split -> weights exp(m_s - M); sm_o is free again.
-        float* sw = sm_o;
-        float* sl = sw + GH * ns;
-        for (int i = threadIdx.x; i < GH * ns; i += kStepThreads) {
-          const int g = i / ns, sp = i % ns;
-          const float* src = p.partials + ((b * hq + kvh * GH + g) * ns + sp) * (d + 2);
-          sw[i] = __ldcg(src + d);
-          sl[i] = __ldcg(src + d + 1);
-        }
-        __syncthreads();
+        float* sw = sm_o;  // free again: weights exp(m_s - M)
         for (int g = warp; g < GH; g += kStepWarps) {
+          const float* ml = p.part_ml + (b * hq + kvh * GH + g) * ns * 4;
           float mx = -INFINITY;
-          for (int sp = lane; sp < ns; sp += 32) mx = fmaxf(mx, sw[g * ns + sp]);
+          for (int sp = lane; sp < ns; sp += 32) mx = fmaxf(mx, __ldcg(ml + sp * 4));
           mx = warp_max_f32(mx);
           float l = 0.0f;
           for (int sp = lane; sp < ns; sp += 32) {
-            const float ms = sw[g * ns + sp];
+            const float ms = __ldcg(ml + sp * 4);
             const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
             sw[g * ns + sp] = f;
-            l = fmaf(sl[g * ns + sp], f, l);
+            l = fmaf(__ldcg(ml + sp * 4 + 1), f, l);
           }
           l = warp_sum_f32(l);
           if (lane == 0) cta_l[g] = l;
@@ -489,35 +546,77 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
           const int g = static_cast<int>(idx / d);
           const int64_t e = idx % d;
           const int64_t row = b * hq + kvh * GH + g;
-          const float* src = p.partials + row * ns * (d + 2) + e;
+          const float* src = p.part_o + row * ns * d + e;
           float o = 0.0f;
 #pragma unroll 8
-          for (int sp = 0; sp < ns; ++sp) o = fmaf(__ldcg(src + sp * (d + 2)), sw[g * ns + sp], o);
+          for (int sp = 0; sp < ns; ++sp) o = fmaf(__ldcg(src + sp * d), sw[g * ns + sp], o);
           p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, cta_l[g]));
         }
+        cta_signal(&sync[kSyncCtxDone]);  // counts (b, kv head) groups
       }
     }
-    if (combine) cta_signal(&sync[kSyncCtxDone]);
+    if (threadIdx.x == 0 && (p.sched & 7) == 2 && has_qkv) issue_o();
     NVFP4DA_PHASE(9);
   }
 
   // ---- O projection
   if (has_o) {
     {
-      const int zero = kSyncCtxDone;
-      cta_wait(sync, &zero, 1, static_cast<unsigned>(nb * hkv), err, p.timeout_ns);
+      const int idx0 = kSyncCtxDone;
+      const unsigned target = p.o_combine ? static_cast<unsigned>(n_units) : static_cast<unsigned>(nb * hkv);
+      cta_wait(sync, &idx0, 1, target, err, p.timeout_ns);
     }
     NVFP4DA_PHASE(10);
-    const uint4 none[NCH] = {};
-    const bool f16 =
-        prep_rows_regs<NCH, false, true>(p.ctx, k, mrows, none, 0.0f, x_stage, x16, escale, redf, redd, nullptr);
+    bool f16;
+    if (p.o_combine) {
+      // Every split's partials in one bulk copy (the QKV/KV region is dead),
+      // then the log-sum-exp combine of reference decoder_attention.py's
+      // softmax, split by split in order, per (row, head) item.
+      float* co = reinterpret_cast<float*>(smem + p.off_comb);
+      const int64_t items = nb * hq;
+      float* cml = co + items * ns * d;
+      if (threadIdx.x == 0) {
+        const uint32_t ob = static_cast<uint32_t>(items * ns * d * 4), mb = static_cast<uint32_t>(items * ns * 16);
+        asm volatile("fence.proxy.async.global;" ::: "memory");  // acquired generic writes -> bulk reads
+        mbar_arrive_expect_tx(&bar_c, ob + mb);
+        bulk_g2s(co, p.part_o, ob, &bar_c);
+        bulk_g2s(cml, p.part_ml, mb, &bar_c);
+      }
+      mbar_wait_bounded(&bar_c, 0, err);
+      for (int64_t it = warp; it < items; it += kStepWarps) {
+        const float* ml = cml + it * ns * 4;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, ml[sp * 4]);
+        float l = 0.0f, o[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
+        const float* ob = co + it * ns * d + lane * EPL;
+        for (int sp = 0; sp < ns; ++sp) {
+          const float ms = ml[sp * 4];
+          const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
+          l = fmaf(ml[sp * 4 + 1], f, l);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) o[e] = fmaf(ob[sp * d + e], f, o[e]);
+        }
+        const int64_t m = it / hq, h = it % hq;
+        uint16_t* dst = x_stage + m * k + h * d + lane * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dst[e] = f32_to_bf16_bits(__fdiv_rn(o[e], l));
+      }
+      __syncthreads();
+      NVFP4DA_PHASE(14);
+      f16 = mma_prepare_f16(x_stage, x16, k, mrows, escale, red_small);
+    } else {
+      const uint4 none[NCH] = {};
+      f16 = prep_rows_regs<NCH, false, true>(p.ctx, k, mrows, none, 0.0f, x_stage, x16, escale, redf, redd, nullptr);
+    }
     mbar_wait_bounded(&bar_o, 0, err);
     NVFP4DA_PHASE(11);
     if (f16)
-      mma_gemv_pass_smem<true, 4>(ow_smem, os_smem, reinterpret_cast<const uint16_t*>(x16), k, p.ro_rows, mrows,
-                                  mred, outv);
+      mma_gemv_pass_smem<true, 4>(ow_smem, os_smem, reinterpret_cast<const uint16_t*>(x16), k, p.o_tile_rows,
+                                  o_valid, mrows, mred, outv);
     else
-      mma_gemv_pass_smem<false, 4>(ow_smem, os_smem, x_stage, k, p.ro_rows, mrows, mred, outv);
+      mma_gemv_pass_smem<false, 4>(ow_smem, os_smem, x_stage, k, p.o_tile_rows, o_valid, mrows, mred, outv);
     const float gamma = *p.gamma[3];
     for (int i = threadIdx.x; i < o_valid * mrows; i += kStepThreads) {
       const int n = i / o_valid, r = i % o_valid;
@@ -530,8 +629,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   // ---- leave; the last CTA out clears the slot's counters for the next launch
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(&sync[kSyncExit], 1u);
+    const unsigned prev = atom_add_acq_rel(&sync[kSyncExit], 1u);
     s_flag = prev == gridDim.x - 1 ? 1u : 0u;
   }
   __syncthreads();

@@ -160,9 +160,12 @@ __device__ __forceinline__ void issue_weight_batch(WeightRegs<NB>& w, const uint
 // Consume a batch: decode in registers, 8 MMAs per step.  `xop` is the
 // activation operand ([mgv][K], f16 or bf16 bits) in shared memory; `s_smem`
 // the CTA's scale rows ([rows][K/16]).
+// `hi_rows`: whether rows g + 8 of the tile hold weights at all (warp-uniform);
+// if not, their decode is skipped and they enter the MMA as zeros.
 template <bool F16, int NB>
 __device__ __forceinline__ void mma_batch(const WeightRegs<NB>& w, const uint8_t* s_smem, const uint16_t* xop,
-                                          int64_t k, int tile, int s, int s_end, int mgv, float (&d)[4][4]) {
+                                          int64_t k, int tile, int s, int s_end, int mgv, float (&d)[4][4],
+                                          bool hi_rows = true) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int64_t ks = k / 16;
   const uint8_t* sc_lo = s_smem + (tile * 16 + g) * ks + 2 * t;
@@ -188,7 +191,7 @@ __device__ __forceinline__ void mma_batch(const WeightRegs<NB>& w, const uint8_t
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         q0[j] = hmul2_u32(e2m1x2_to_f16x2(wl[p] >> (8 * j)), blo[p >> 1]);
-        q1[j] = hmul2_u32(e2m1x2_to_f16x2(wh[p] >> (8 * j)), bhi[p >> 1]);
+        q1[j] = hi_rows ? hmul2_u32(e2m1x2_to_f16x2(wh[p] >> (8 * j)), bhi[p >> 1]) : 0u;
       }
       if constexpr (F16) {
         const uint32_t a_lo[4] = {q0[0], q1[0], q0[1], q1[1]};
@@ -267,15 +270,22 @@ __device__ __forceinline__ void load_weight_batch_smem(WeightRegs<NB>& w, const 
   }
 }
 
+// `rows` is tile-padded (16 x 1/2/4/8); tiles or tile halves at or past
+// `valid_rows` are skipped (their outputs are undefined).
 template <bool F16, int NB>
 __device__ __forceinline__ void mma_gemv_pass_smem(const uint8_t* w_smem, const uint8_t* s_smem, const uint16_t* xop,
-                                                   int64_t k, int rows, int mgv, float* red, float* out) {
+                                                   int64_t k, int rows, int valid_rows, int mgv, float* red,
+                                                   float* out) {
   const WarpSlice ws = warp_slice(rows, k);
   float d[4][4] = {};
-  for (int s = ws.s0; s < ws.s1; s += NB) {
-    WeightRegs<NB> w;
-    load_weight_batch_smem<NB>(w, w_smem, k, ws.tile, s, ws.s1);
-    mma_batch<F16, NB>(w, s_smem, xop, k, ws.tile, s, ws.s1, mgv, d);
+  if (ws.tile * 16 < valid_rows) {
+    const bool hi = ws.tile * 16 + 8 < valid_rows;
+#pragma unroll 1
+    for (int s = ws.s0; s < ws.s1; s += NB) {
+      WeightRegs<NB> w;
+      load_weight_batch_smem<NB>(w, w_smem, k, ws.tile, s, ws.s1);
+      mma_batch<F16, NB>(w, s_smem, xop, k, ws.tile, s, ws.s1, mgv, d, hi);
+    }
   }
   float dsum[4];
 #pragma unroll

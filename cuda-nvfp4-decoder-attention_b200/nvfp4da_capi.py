@@ -224,7 +224,10 @@ class Forward:
                  stages: dict[str, torch.Tensor] | None = None):
         b, t, h = x.shape
         _, hkv, c, d = k_cache.shape
-        self._keep = [x, input_norm_weight, q_norm_weight, k_norm_weight, k_cache, v_cache, output, past_lengths]
+        # The C arguments hold raw pointers: keep every tensor they point into
+        # (weights included) alive as long as this object.
+        self._keep = [x, input_norm_weight, q_norm_weight, k_norm_weight, k_cache, v_cache, output, past_lengths,
+                      q_w, k_w, v_w, o_w]
         self.args = ForwardArgs()
         a = self.args
         a.x, a.input_norm_weight = x.data_ptr(), input_norm_weight.data_ptr()

@@ -153,10 +153,10 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* wo
                                       void* stream);
 
 /* Forward with an explicit kernel path.  NVFP4DA_PATH_AUTO (what
- * nvfp4da_decoder_attention_forward uses) takes the one-kernel decode step
- * when it covers the call, else the three-kernel chain; NVFP4DA_PATH_CHAIN
- * always takes the chain; NVFP4DA_PATH_STEP takes the one-kernel step or fails
- * with NVFP4DA_ERR_UNSUPPORTED.  Same results within the numerics policy (the
+ * nvfp4da_decoder_attention_forward uses) takes the faster path for the call
+ * as measured on B200 (currently the three-kernel chain everywhere);
+ * NVFP4DA_PATH_CHAIN always takes the chain; NVFP4DA_PATH_STEP takes the
+ * one-kernel decode step or fails with NVFP4DA_ERR_UNSUPPORTED.  Same results within the numerics policy (the
  * FP32 summation order of the projections and of the attention splits
  * differs).  The one-kernel step covers T == 1, B <= 8, hidden % 256 == 0,
  * hidden <= 4096, head_dim in {64, 128, 256}, 1/2/4/8 query heads per KV head,
