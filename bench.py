@@ -70,6 +70,19 @@ def step_bytes(shape) -> dict:
     return {"qkv": qkv, "attention": attn, "o_proj": o, "step": total}
 
 
+def ncu_traffic(kernel: str) -> float | None:
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
+    summary (profiles/<kernel>_canonical.md, line `dram_bytes_per_launch: N`)."""
+    import re
+
+    p = ROOT / "profiles" / f"{kernel}_canonical.md"
+    try:
+        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
 def measured_peak_gbs() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -315,7 +328,9 @@ def run_gpu(args) -> None:
         "roofline": {"bound": "hbm", "kernel": "qkv_fused (input norm + W4A16 QKV + head norm + RoPE + append)",
                      "achieved": round(qkv_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(qkv_gbs / peak, 4), "peak_source": peak_src,
-                     "traffic": None,
+                     "traffic": ncu_traffic("qkv_fused"),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                       "(profiles/qkv_fused_canonical.md)",
                      "bytes_per_launch": nbytes["qkv"],
                      "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
                      "step_bytes": nbytes["step"]},
