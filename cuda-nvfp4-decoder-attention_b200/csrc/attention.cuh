@@ -49,7 +49,30 @@ struct AttnParams {
   int pdl;
   int cluster_combine;  // 1: the `splits` CTAs of a (b, t, head group) form one
                         // thread-block cluster and combine through DSMEM
+  // KV-length sharding: the caches hold global positions [pos_offset,
+  // pos_offset + capacity) of each sequence; a query at global position P_b + t
+  // sees the local slots below P_b + t + 1 - pos_offset.  With out_partial set,
+  // the result is this shard's log-sum-exp partial instead of the context:
+  // out_partial[row][0..D) = sum_j exp(s_j - m) v_j (unnormalised), [D] = m,
+  // [D + 1] = l = sum_j exp(s_j - m); a shard with no visible key gives
+  // m = -inf, l = 0, o = 0.
+  int64_t pos_offset;
+  float* out_partial;  // [B*T*Hq][D + 2] or nullptr
 };
+
+// Final write of one (row, element): the BF16 context, or the shard partial.
+__device__ __forceinline__ void attn_store(const AttnParams& p, int64_t row, int64_t e, float o, float m, float l) {
+  if (p.out_partial) {
+    float* dst = p.out_partial + row * (p.head_dim + 2);
+    dst[e] = o;
+    if (e == 0) {
+      dst[p.head_dim] = m;
+      dst[p.head_dim + 1] = l;
+    }
+  } else {
+    p.ctx[row * p.head_dim + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
+  }
+}
 
 template <int EPL>
 __device__ __forceinline__ void load_row(const uint16_t* row, int lane, int64_t d, float (&out)[EPL]) {
@@ -129,7 +152,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
 
   // Keys 0 .. P_b + t; never read beyond the physical capacity, whatever a
   // device-side length says.
-  const int64_t pb = seq_past(p, b);
+  const int64_t pb = seq_past(p, b) - p.pos_offset;  // this shard's slot of position P_b
   int64_t visible = pb + t + 1;
   if (visible > p.capacity) visible = p.capacity;
   const int64_t s0 = static_cast<int64_t>(split) * p.split_len;
@@ -290,7 +313,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     if (e >= d) continue;
     const int64_t row = bt * p.q_heads + h0 + g;
     if (single) {
-      p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, cta_l[g]));
+      attn_store(p, row, e, o, cta_m[g], cta_l[g]);
     } else {
       float* dst = part_base + (row * p.splits + split) * (d + 2);
       dst[e] = o;
@@ -312,7 +335,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     cg::cluster_group cluster = cg::this_cluster();
     const int ns = static_cast<int>(cluster.num_blocks());
     const int rank = static_cast<int>(cluster.block_rank());
-    __shared__ float rw[16][GH], rl[16][GH], head_inv_l[GH];
+    __shared__ float rw[16][GH], rl[16][GH], head_inv_l[GH], head_mx[GH];
     NVFP4DA_PHASE(4);
     cluster.sync();
     NVFP4DA_PHASE(5);
@@ -333,6 +356,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
         l = fmaf(rl[r][g], f, l);
       }
       head_inv_l[g] = l;
+      head_mx[g] = mx;
     }
     __syncthreads();
     const int total = GH * static_cast<int>(d);
@@ -347,7 +371,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
 #pragma unroll
       for (int r = 0; r < 16; ++r)
         if (r < ns) o = fmaf(vals[r], rw[r][g], o);
-      p.ctx[(bt * p.q_heads + h0 + g) * d + e] = f32_to_bf16_bits(__fdiv_rn(o, head_inv_l[g]));
+      attn_store(p, bt * p.q_heads + h0 + g, e, o, head_mx[g], head_inv_l[g]);
     }
     NVFP4DA_PHASE(6);
     cluster.sync();  // keep this CTA's shared memory alive until its peers are done
@@ -357,7 +381,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
 
   // ---- last CTA of this (b, t, head group) combines all splits.
   __shared__ unsigned s_last;
-  __shared__ float head_l[GH];
+  __shared__ float head_l[GH], head_m[GH];
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -394,7 +418,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
       l = fmaf(sl[g * ns + sp], f, l);
     }
     l = warp_sum_f32(l);
-    if (lane == 0) head_l[g] = l;
+    if (lane == 0) {
+      head_l[g] = l;
+      head_m[g] = mx;
+    }
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < GH * d; idx += kAttnThreads) {
@@ -405,7 +432,35 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     float o = 0.0f;
 #pragma unroll 8
     for (int sp = 0; sp < ns; ++sp) o = fmaf(__ldcg(src + sp * (d + 2)), sw[g * ns + sp], o);
-    p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, head_l[g]));
+    attn_store(p, row, e, o, head_m[g], head_l[g]);
+  }
+}
+
+// Log-sum-exp combine of the per-shard partials of KV-length-sharded
+// attention: partials [G][rows][D + 2] (o unnormalised, m, l) ->
+// ctx[rows][D] = BF16( sum_r o_r e^(m_r - M) / sum_r l_r e^(m_r - M) ),
+// shards in order.  One warp per row.
+__global__ void attn_combine_kernel(const float* partials, int shards, int64_t rows, int64_t d, uint16_t* ctx) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t stride = rows * (d + 2);
+  float mx = -INFINITY;
+  for (int r = 0; r < shards; ++r) mx = fmaxf(mx, partials[r * stride + row * (d + 2) + d]);
+  float l = 0.0f;
+  for (int r = 0; r < shards; ++r) {
+    const float* src = partials + r * stride + row * (d + 2);
+    const float f = (src[d] == -INFINITY) ? 0.0f : expf(src[d] - mx);
+    l = fmaf(src[d + 1], f, l);
+  }
+  for (int64_t e = lane; e < d; e += 32) {
+    float o = 0.0f;
+    for (int r = 0; r < shards; ++r) {
+      const float* src = partials + r * stride + row * (d + 2);
+      const float f = (src[d] == -INFINITY) ? 0.0f : expf(src[d] - mx);
+      o = fmaf(src[e], f, o);
+    }
+    ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, l));
   }
 }
 

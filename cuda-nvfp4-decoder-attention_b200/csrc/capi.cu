@@ -350,7 +350,8 @@ int check_attention_dims(int64_t batch, int64_t tokens, int64_t q_heads, int64_t
 int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* ctx, int64_t batch,
                   int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t capacity, int64_t head_dim,
                   int64_t past_length, const int64_t* past_lengths, int64_t max_past, void* ws, size_t ws_bytes,
-                  cudaStream_t s, bool pdl, bool clear_counters) {
+                  cudaStream_t s, bool pdl, bool clear_counters, int64_t pos_offset = 0,
+                  float* out_partial = nullptr) {
   AttnPlan pl;
   if (!plan_attention(batch, tokens, q_heads, kv_heads, head_dim, max_past, pl))
     return fail(NVFP4DA_ERR_UNSUPPORTED, "head_dim %lld is not supported (need head_dim <= 256 and divisible by "
@@ -380,6 +381,8 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
   p.counters = global ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pl.partial_bytes) : nullptr;
   p.pdl = pdl ? 1 : 0;
   p.cluster_combine = pl.cluster ? 1 : 0;
+  p.pos_offset = pos_offset;
+  p.out_partial = out_partial;
   if (clear_counters && global) {
     cudaError_t e = cudaMemsetAsync(p.counters, 0, pl.counter_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "attention counter clear");
@@ -1130,6 +1133,83 @@ int nvfp4da_debug_wait_timeout(void* stream, unsigned long long timeout_ns, unsi
   e = cudaMemcpyAsync(flags, static_cast<unsigned*>(words) + 1, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   return e == cudaSuccess ? NVFP4DA_OK : cuda_fail(e, "probe read");
+}
+
+// ---------------------------------------------------------------- KV-length sharding
+// A shard holds global positions [shard_start, shard_start + capacity) of every
+// sequence; plan its attention over the keys it can see.
+static int64_t shard_visible_max(int64_t max_past, int64_t tokens, int64_t shard_start, int64_t capacity) {
+  int64_t v = max_past + tokens - shard_start;
+  if (v > capacity) v = capacity;
+  return v < 1 ? 1 : v;
+}
+
+int nvfp4da_qkv_rope_append_shard(const nvfp4da_forward_args* a, int64_t shard_start, int64_t global_capacity,
+                                  uint16_t* q_rope_out, void* stream) {
+  if (!a) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (shard_start < 0 || a->capacity <= 0 || global_capacity <= 0 ||
+      shard_start > global_capacity - a->capacity)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "shard [%lld, %lld) is not inside the cache capacity %lld",
+                static_cast<long long>(shard_start), static_cast<long long>(shard_start + a->capacity),
+                static_cast<long long>(global_capacity));
+  nvfp4da_forward_args g = *a;  // validate against the whole (global) cache
+  g.capacity = global_capacity;
+  int r = check_forward(&g);
+  if (r) return r;
+  if (!q_rope_out) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "q_rope_out is NULL");
+  QkvPlan pl;
+  if (!plan_qkv(a->batch * a->tokens, a->hidden, a->head_dim, pl))
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "the fused QKV kernel needs head_dim %% 32 == 0, head_dim <= 256 and hidden %% 128 == 0");
+  QkvParams p = qkv_params(a, q_rope_out);
+  p.slot_offset = shard_start;
+  const int64_t hq = a->hidden / a->head_dim;
+  cudaError_t e = launch_qkv(p, pl, hq + 2 * a->kv_heads, static_cast<cudaStream_t>(stream), true);
+  if (e != cudaSuccess) return cuda_fail(e, "fused qkv launch");
+  return NVFP4DA_OK;
+}
+
+size_t nvfp4da_gqa_attention_partials_workspace_size(int64_t batch, int64_t tokens, int64_t q_heads,
+                                                     int64_t kv_heads, int64_t head_dim, int64_t shard_start,
+                                                     int64_t shard_capacity, int64_t max_past_length) {
+  AttnPlan pl;
+  if (batch <= 0 || tokens <= 0 || kv_heads <= 0 || q_heads % kv_heads || shard_capacity <= 0 ||
+      !plan_attention(batch, tokens, q_heads, kv_heads, head_dim,
+                      shard_visible_max(max_past_length, tokens, shard_start, shard_capacity) - tokens, pl))
+    return 0;
+  return std::max<size_t>(256, pl.partial_bytes + pl.counter_bytes);
+}
+
+int nvfp4da_gqa_attention_partials(const uint16_t* q, const uint16_t* k_shard, const uint16_t* v_shard,
+                                   float* partials, int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads,
+                                   int64_t shard_capacity, int64_t head_dim, int64_t shard_start,
+                                   int64_t past_length, const int64_t* past_lengths, int64_t max_past_length,
+                                   void* ws, size_t ws_bytes, void* stream) {
+  if (!q || !k_shard || !v_shard || !partials) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "attention partials: NULL pointer");
+  if (!past_lengths) max_past_length = past_length;
+  if (shard_start < 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "shard_start must be nonnegative");
+  // Dimensions as for one cache of capacity shard_start + shard_capacity.
+  int r = check_attention_dims(batch, tokens, q_heads, kv_heads,
+                               std::max<int64_t>(shard_start + shard_capacity, max_past_length + tokens), head_dim,
+                               max_past_length);
+  if (r) return r;
+  if (!aligned(q, 16) || !aligned(k_shard, 16) || !aligned(v_shard, 16) || !aligned(partials, 16))
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "attention tensors must be 16-byte aligned");
+  const int64_t vis = shard_visible_max(max_past_length, tokens, shard_start, shard_capacity);
+  return run_attention(q, k_shard, v_shard, nullptr, batch, tokens, q_heads, kv_heads, shard_capacity, head_dim,
+                       past_length, past_lengths, vis - tokens, ws, ws_bytes, static_cast<cudaStream_t>(stream),
+                       false, true, shard_start, partials);
+}
+
+int nvfp4da_attention_combine(const float* partials, int shards, int64_t rows, int64_t head_dim, uint16_t* ctx,
+                              void* stream) {
+  if (!partials || !ctx || shards <= 0 || rows <= 0 || head_dim <= 0)
+    return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "attention combine: invalid arguments");
+  if (ceil_div(rows, 8) > std::numeric_limits<int32_t>::max())
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "too many rows for a one-dimensional grid");
+  attn_combine_kernel<<<static_cast<unsigned>(ceil_div(rows, 8)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      partials, shards, rows, head_dim, ctx);
+  NVFP4DA_CHECK_LAUNCH("attention combine launch");
+  return NVFP4DA_OK;
 }
 
 #ifdef NVFP4DA_PHASES

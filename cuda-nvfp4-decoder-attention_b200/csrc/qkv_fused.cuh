@@ -55,6 +55,10 @@ struct QkvParams {
   int64_t n_zero_words;
   unsigned* err;
   int pdl;
+  // KV-length sharding: the caches hold positions [slot_offset, slot_offset +
+  // capacity); a position outside that range is not appended here (RoPE still
+  // uses the global position).
+  int64_t slot_offset;
   // RoPE cos/sin per token index t < rope_rows, computed on the host when the
   // positions are the scalar past_length + t (rope_rows == 0: on the device).
   int rope_rows;
@@ -301,10 +305,11 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
       // A per-sequence length read from device memory cannot be checked on the
       // host: a slot outside [0, C) is not written (the caller's contract is
       // 0 <= P_b and P_b + T <= C).
-      const bool slot_ok = pos >= 0 && pos < p.capacity;
+      const int64_t slot = pos - p.slot_offset;  // cache slot of this position in this shard
+      const bool slot_ok = slot >= 0 && slot < p.capacity;
       const uint16_t* y = head_out[warp];
       if (mat == 2) {
-        uint16_t* dst = slot_ok ? p.v_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d : nullptr;
+        uint16_t* dst = slot_ok ? p.v_cache + ((b * p.kv_heads + head) * p.capacity + slot) * d : nullptr;
         for (int64_t e = lane; e < d; e += 32) {
           if (dst) dst[e] = y[e];
           if (p.dbg_v) p.dbg_v[mrow * p.kv_heads * d + head * d + e] = y[e];
@@ -322,7 +327,7 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
         uint16_t* dbg_proj = (mat == 0) ? p.dbg_q : p.dbg_k;
         uint16_t* dbg_norm = (mat == 0) ? p.dbg_qn : p.dbg_kn;
         uint16_t* dst = (mat == 0) ? p.q_out + (mrow * p.q_heads + head) * d
-                        : slot_ok  ? p.k_cache + ((b * p.kv_heads + head) * p.capacity + pos) * d
+                        : slot_ok  ? p.k_cache + ((b * p.kv_heads + head) * p.capacity + slot) * d
                                    : nullptr;
         for (int64_t pr = lane; pr < d / 2; pr += 32) {
           const int64_t e = 2 * pr;

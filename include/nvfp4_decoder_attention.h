@@ -190,6 +190,36 @@ int nvfp4da_debug_wait_timeout(void* stream, unsigned long long timeout_ns, unsi
  * args->output are not used.  Needs head_dim % 32 == 0 and head_dim <= 256. */
 int nvfp4da_qkv_rope_append(const nvfp4da_forward_args* args, uint16_t* q_rope_out, void* stream);
 
+/* ---- KV-length sharding (long-context decode over several GPUs).  Each
+ * GPU holds the positions [shard_start, shard_start + shard_capacity) of every
+ * sequence's cache ([B, Hkv, shard_capacity, D]).  One step:
+ *   1. nvfp4da_qkv_rope_append_shard on every GPU (replicated projections;
+ *      only the GPU whose shard holds slot P_b + t appends it);
+ *   2. nvfp4da_gqa_attention_partials: this shard's log-sum-exp partials;
+ *   3. an all-gather of the partials between the GPUs (the host's NCCL
+ *      communicator), then nvfp4da_attention_combine -> context;
+ *   4. nvfp4da_w4a16_linear with the O weight.
+ * Replaces the single-GPU cuda_gqa_attention_cached path for caches split by
+ * position; the reference has no multi-GPU path. */
+/* Step 1: as nvfp4da_qkv_rope_append, with args->k_cache / v_cache this
+ * shard's caches and args->capacity the shard capacity; positions are checked
+ * against global_capacity; RoPE uses the global position. */
+int nvfp4da_qkv_rope_append_shard(const nvfp4da_forward_args* args, int64_t shard_start, int64_t global_capacity,
+                                  uint16_t* q_rope_out, void* stream);
+/* Step 2: partials [B*T*Hq][D + 2] float32: o (unnormalised), m, l per query
+ * row; a shard with no visible key gives m = -inf, l = 0, o = 0. */
+size_t nvfp4da_gqa_attention_partials_workspace_size(int64_t batch, int64_t tokens, int64_t q_heads,
+                                                     int64_t kv_heads, int64_t head_dim, int64_t shard_start,
+                                                     int64_t shard_capacity, int64_t max_past_length);
+int nvfp4da_gqa_attention_partials(const uint16_t* q, const uint16_t* k_shard, const uint16_t* v_shard,
+                                   float* partials, int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads,
+                                   int64_t shard_capacity, int64_t head_dim, int64_t shard_start,
+                                   int64_t past_length, const int64_t* past_lengths, int64_t max_past_length,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+/* Step 3: partials [shards][rows][D + 2] (shard order) -> BF16 context
+ * [rows][D], rows = B*T*Hq. */
+int nvfp4da_attention_combine(const float* partials, int shards, int64_t rows, int64_t head_dim, uint16_t* ctx,
+                              void* stream);
 /* Allocation-free forward.  No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (a fixed HBM budget reserved up
  * front, a host whose allocator owns all device memory, or a context where an
