@@ -70,6 +70,16 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte_in_low_bits) {
   return out;
 }
 
+// Four packed bytes -> four f16x2 (byte j -> out[j], low nibble in the low
+// half).  The bytes are unpacked by one mov, so no shifts are issued.
+__device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t (&o)[4]) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w));
+}
+
 // Decode four packed bytes (eight nibbles, k = 0..7 in order) to FP32.
 __device__ __forceinline__ void decode8_e2m1(uint32_t word, float (&out)[8]) {
 #pragma unroll

@@ -188,10 +188,12 @@ __device__ __forceinline__ void mma_batch(const WeightRegs<NB>& w, const uint8_t
       uint4 xb = make_uint4(0u, 0u, 0u, 0u);
       if (has_n) xb = *reinterpret_cast<const uint4*>(xrow + st * kStepK + 8 * p);
       uint32_t q0[4], q1[4];  // rows g / g+8: nibble pairs of word p
+      e2m1x8_to_f16x2x4(wl[p], q0);
+      if (hi_rows) e2m1x8_to_f16x2x4(wh[p], q1);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        q0[j] = hmul2_u32(e2m1x2_to_f16x2(wl[p] >> (8 * j)), blo[p >> 1]);
-        q1[j] = hi_rows ? hmul2_u32(e2m1x2_to_f16x2(wh[p] >> (8 * j)), bhi[p >> 1]) : 0u;
+        q0[j] = hmul2_u32(q0[j], blo[p >> 1]);
+        q1[j] = hi_rows ? hmul2_u32(q1[j], bhi[p >> 1]) : 0u;
       }
       if constexpr (F16) {
         const uint32_t a_lo[4] = {q0[0], q1[0], q0[1], q1[1]};
