@@ -1,6 +1,7 @@
 // C ABI of libnvfp4da.so: validation, launch planning and kernel launches.
 // Declarations and reference citations: include/nvfp4_decoder_attention.h.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -18,6 +19,7 @@
 #include "attention.cuh"
 #include "elementwise.cuh"
 #include "gemv_kernel.cuh"
+#include "prefill_gemm.cuh"
 #include "decode_step.cuh"
 #include "qkv_fused.cuh"
 
@@ -155,6 +157,10 @@ int check_weight(const nvfp4da_weight* w, const char* name) {
   return NVFP4DA_OK;
 }
 
+bool gemm_tc_supported(const uint16_t* x, int64_t m, const nvfp4da_weight& w, const uint16_t* y);
+int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s);
+constexpr int64_t kGemmMinMDecl = 64;  // at and above this M the tensor-core GEMM replaces the GEMV
+
 // ---------------------------------------------------------------- GEMV plan
 struct GemvPlan {
   bool mma;      // tensor-core path (K % 32 == 0)
@@ -229,6 +235,7 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStream_t s,
 }
 
 int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s, bool pdl) {
+  if (m >= kGemmMinMDecl && gemm_tc_supported(x, m, w, y)) return run_gemm_tc(x, m, w, y, s);
   GemvPlan pl;
   if (!plan_gemv(m, w.rows, w.cols, pl))
     return fail(NVFP4DA_ERR_UNSUPPORTED, "K=%lld is too large for the shared-memory GEMV", static_cast<long long>(w.cols));
@@ -237,6 +244,65 @@ int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y,
   GemvParams p{x, m, w.packed_values, w.block_scales, w.global_decode_scale, y, w.rows, w.cols, nullptr, pdl ? 1 : 0};
   cudaError_t e = launch_gemv(p, pl, s, pdl);
   if (e != cudaSuccess) return cuda_fail(e, "w4a16 gemv launch");
+  return NVFP4DA_OK;
+}
+
+// ---------------------------------------------------------------- tensor-core GEMM (prefill-sized M)
+constexpr int kPgBN = 128;
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tensor-core path needs whole 64-wide K steps and 16-byte TMA row
+// strides for the scales (K % 256 == 0), and 16-byte aligned bases.
+bool gemm_tc_supported(const uint16_t* x, int64_t m, const nvfp4da_weight& w, const uint16_t* y) {
+  return w.cols >= 256 && w.cols % 256 == 0 && m > 0 && aligned(x, 16) && aligned(y, 2) &&
+         aligned(w.packed_values, 16) && aligned(w.block_scales, 16) && m <= (int64_t(1) << 31) &&
+         w.rows <= (int64_t(1) << 31) && tensor_map_encoder() != nullptr;
+}
+
+int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s) {
+  const int64_t n = w.rows, k = w.cols;
+  CUtensorMap tx, tw, ts;
+  if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m, k * 2, kPgBK, kPgBM,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed_values, k / 2, n, k / 2, kPgBK / 2, kPgBN,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.block_scales, k / 16, n, k / 16, 16, kPgBN,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+    return fail(NVFP4DA_ERR_CUDA, "tensor map encoding failed for the tensor-core GEMM");
+  PgParams p{m, n, k, w.global_decode_scale, y, nullptr};
+  auto* kern = w4a16_gemm_tc_kernel<kPgBN>;
+  const uint32_t smem = PgLayout<kPgBN>::total();
+  cudaError_t e = ensure_smem(kern, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM shared-memory opt-in");
+  const dim3 grid(static_cast<unsigned>(ceil_div(n, kPgBN)), static_cast<unsigned>(ceil_div(m, kPgBM)));
+  if (grid.y > 65535) return fail(NVFP4DA_ERR_UNSUPPORTED, "M too large for the tensor-core GEMM grid");
+  kern<<<grid, kPgThreads, smem, s>>>(tx, tw, ts, p);
+  NVFP4DA_CHECK_LAUNCH("tensor-core GEMM launch");
   return NVFP4DA_OK;
 }
 
@@ -971,6 +1037,15 @@ int nvfp4da_w4a16_linear(const uint16_t* x, int64_t m, const nvfp4da_weight* w, 
   if (r) return r;
   if (!x || !y || m <= 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "w4a16_linear: invalid arguments");
   return run_gemv(x, m, *w, y, static_cast<cudaStream_t>(stream), false);
+}
+
+int nvfp4da_w4a16_gemm(const uint16_t* x, int64_t m, const nvfp4da_weight* w, uint16_t* y, void* stream) {
+  int r = check_weight(w, "weight");
+  if (r) return r;
+  if (!x || !y || m <= 0) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "w4a16_gemm: invalid arguments");
+  if (!gemm_tc_supported(x, m, *w, y))
+    return fail(NVFP4DA_ERR_UNSUPPORTED, "the tensor-core GEMM needs K %% 256 == 0 and 16-byte aligned operands");
+  return run_gemm_tc(x, m, *w, y, static_cast<cudaStream_t>(stream));
 }
 
 int nvfp4da_kv_cache_append(uint16_t* kc, uint16_t* vc, const uint16_t* nk, const uint16_t* nv, int64_t batch,

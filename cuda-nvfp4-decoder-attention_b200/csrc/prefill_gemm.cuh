@@ -1,0 +1,282 @@
+// W4A16 dense projection for prefill-sized M on the 5th-generation tensor
+// cores: y[M, N] = BF16( gamma * sum_k x[m, k] * (q * beta)[n, k] ).
+//
+// Semantics: reference/w4a16.py:11-59 (x @ W_hat.T with W_hat = (q*beta)*gamma,
+// FP32 accumulation, BF16 output).  q*beta has at most 6 significant bits and
+// lies in [2^-10, 2688], so it is exact in BF16; BF16 x BF16 products are exact
+// in the FP32 accumulator, and gamma is applied once in the epilogue.
+//
+// One CTA computes a 128 x BN tile of y with tcgen05.mma (kind::f16, BF16
+// operands, FP32 accumulators in tensor memory), K in steps of 64:
+//  * x tile [128 rows x 64 k] by TMA with 128-byte swizzle (the canonical
+//    K-major SW128 operand layout), the packed weight tile [BN x 32 bytes] and,
+//    every 4 steps, the scale tile [BN x 16 bytes] by TMA, double-buffered on
+//    mbarriers;
+//  * the 128 threads decode the weight tile (one row each: E2M1 -> f16 by the
+//    hardware conversion, times the UE4M3 scale, -> BF16, all exact) into the
+//    SW128 K-major layout in shared memory;
+//  * one thread issues the four K=16 MMAs of the step and commits them to the
+//    stage's mbarrier, which frees the stage for the loads two steps ahead;
+//  * epilogue: each warp reads its 32 accumulator lanes (rows) with
+//    tcgen05.ld, scales by gamma and stores BF16.
+// Every wait is bounded; on expiry the kernel records kErrBarrierTimeout,
+// skips the remaining work, and still frees its tensor memory.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace nvfp4da {
+
+constexpr int kPgBM = 128;
+constexpr int kPgBK = 64;
+constexpr int kPgThreads = 128;
+// K steps go round-robin to kPgAcc accumulators (TMEM column blocks) that the
+// epilogue adds in FP32: shorter accumulation chains keep the tensor cores'
+// internal rounding within one BF16 step of the correctly rounded sum.
+constexpr int kPgAcc = 4;
+
+struct PgParams {
+  int64_t m, n, k;
+  const float* gamma;
+  uint16_t* y;  // [M, N]
+  unsigned* err;
+};
+
+// Shared-memory layout of one CTA (byte offsets from a 1024-aligned base).
+template <int BN>
+struct PgLayout {
+  static constexpr uint32_t kA = kPgBM * kPgBK * 2;  // 16 KB per stage
+  static constexpr uint32_t kB = BN * kPgBK * 2;     // decoded weight tile per stage
+  static constexpr uint32_t kW = BN * kPgBK / 2;     // packed weight tile per stage
+  static constexpr uint32_t kS = BN * 16;            // scales of 4 steps
+  __host__ __device__ static constexpr uint32_t a(int s) { return s * kA; }
+  __host__ __device__ static constexpr uint32_t b(int s) { return 2 * kA + s * kB; }
+  __host__ __device__ static constexpr uint32_t w(int s) { return 2 * kA + 2 * kB + s * kW; }
+  __host__ __device__ static constexpr uint32_t sc(int s) { return 2 * kA + 2 * kB + 2 * kW + s * kS; }
+  // + 1024 alignment slack; at least 116 KB so that one CTA (which holds all
+  // 512 tensor-memory columns) runs per SM.
+  __host__ __device__ static constexpr uint32_t used() { return 2 * kA + 2 * kB + 2 * kW + 2 * kS + 1024; }
+  __host__ __device__ static constexpr uint32_t total() { return used() > 116u * 1024 ? used() : 116u * 1024; }
+};
+
+// ---------------------------------------------------------------- tcgen05 / TMA primitives
+// Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
+// start address >> 4 (bits 0-13), leading byte offset (unused for swizzled
+// K-major, 16 B), stride byte offset 1024 B = 8 rows x 128 B (bits 32-45),
+// descriptor version 1 (bits 46-47), swizzle mode 2 = 128 B (bits 61-63).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor, kind::f16: FP32 D (bits 4-5 = 1), BF16 A and B
+// (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at 24-28.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Exact f16x2 -> bf16x2 for the decoded weights (at most 6 significant bits).
+__device__ __forceinline__ uint32_t f16x2_to_bf16x2_exact(uint32_t h) {
+  float lo, hi;
+  asm("{\n .reg .b16 l, u;\n mov.b32 {l, u}, %2;\n cvt.f32.f16 %0, l;\n cvt.f32.f16 %1, u;\n}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(h));
+  uint32_t out;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
+  return out;
+}
+
+// ---------------------------------------------------------------- the kernel
+template <int BN>
+__global__ void __launch_bounds__(kPgThreads, 1)
+    w4a16_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                         const __grid_constant__ CUtensorMap tm_s, PgParams p) {
+  using L = PgLayout<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_load[2], bar_mma[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ unsigned s_bad;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = blockIdx.y * kPgBM, n0 = blockIdx.x * BN;
+  const int nk = static_cast<int>(p.k / kPgBK);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(BN * kPgAcc)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_load[s], 1);
+      mbar_init(&bar_mma[s], 1);
+    }
+    fence_mbar_init();
+    s_bad = 0u;
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  auto issue = [&](int kt) {
+    const int st = kt & 1;
+    const bool with_scales = (kt & 3) == 0;
+    mbar_arrive_expect_tx(&bar_load[st], L::kA + L::kW + (with_scales ? L::kS : 0u));
+    tma_load_2d(smem + L::a(st), &tm_x, kt * kPgBK, m0, &bar_load[st]);
+    tma_load_2d(smem + L::w(st), &tm_w, kt * (kPgBK / 2), n0, &bar_load[st]);
+    if (with_scales) tma_load_2d(smem + L::sc((kt >> 2) & 1), &tm_s, kt * (kPgBK / 16), n0, &bar_load[st]);
+  };
+  if (tid == 0) issue(0);
+
+  constexpr uint32_t kIdesc = umma_idesc_bf16(kPgBM, BN);
+  for (int kt = 0; kt < nk; ++kt) {
+    const int st = kt & 1;
+    if (kt + 1 < nk) {
+      // Stage (kt + 1) & 1 was last read by the MMAs of step kt - 1.
+      if (kt >= 1 && !mbar_wait_bounded(&bar_mma[(kt + 1) & 1], ((kt - 1) >> 1) & 1, p.err)) s_bad = 1u;
+      if (tid == 0) issue(kt + 1);
+    }
+    if (!mbar_wait_bounded(&bar_load[st], (kt >> 1) & 1, p.err)) s_bad = 1u;
+    __syncthreads();
+    if (s_bad) break;
+    // ---- decode this thread's weight row for k-step kt into the SW128 layout
+    if (tid < BN) {
+      const int row = tid;
+      const uint4* wp = reinterpret_cast<const uint4*>(smem + L::w(st) + row * (kPgBK / 2));
+      const uint4 w01 = wp[0], w23 = wp[1];
+      const uint32_t words[8] = {w01.x, w01.y, w01.z, w01.w, w23.x, w23.y, w23.z, w23.w};
+      const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(smem + L::sc((kt >> 2) & 1) + row * 16 + (kt & 3) * 4);
+      uint8_t* brow = smem + L::b(st) + row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // chunk c = 8 k = word c
+        uint32_t beta;
+        asm("{\n .reg .b16 lo;\n cvt.u16.u32 lo, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}"
+            : "=r"(beta)
+            : "r"((sc4 >> (8 * (c >> 1))) & 0xffu));
+        beta = __byte_perm(beta, 0, 0x1010);
+        uint32_t h[4];
+        e2m1x8_to_f16x2x4(words[c], h);
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __half2 q = __hmul2(*reinterpret_cast<const __half2*>(&h[j]), *reinterpret_cast<const __half2*>(&beta));
+          o[j] = f16x2_to_bf16x2_exact(*reinterpret_cast<const uint32_t*>(&q));
+        }
+        *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t ad = umma_desc_sw128(smem_u32(smem + L::a(st)));
+      const uint64_t bd = umma_desc_sw128(smem_u32(smem + L::b(st)));
+      const uint32_t acc = tmem + static_cast<uint32_t>((kt % kPgAcc) * BN);
+#pragma unroll
+      for (int kk = 0; kk < kPgBK / 16; ++kk)  // +32 bytes of K per MMA inside the swizzle atom
+        umma_bf16(acc, ad + 2 * kk, bd + 2 * kk, kIdesc, (kt >= kPgAcc || kk > 0) ? 1u : 0u);
+      umma_commit(&bar_mma[st]);
+    }
+  }
+
+  // ---- epilogue: accumulator lanes = tile rows
+  if (!s_bad && nk > 0 && !mbar_wait_bounded(&bar_mma[(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.err)) s_bad = 1u;
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (!s_bad) {
+    const float gamma = *p.gamma;
+    const int64_t row = m0 + warp * 32 + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
+      // Sum the accumulators that received K steps: ((a0 + a1) + (a2 + a3)).
+      if (nk > 1) {
+        uint32_t v1[32];
+        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + BN + c0, v1);
+        if (nk > 2) {
+          uint32_t v2[32], v3[32];
+          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 2 * BN + c0, v2);
+          if (nk > 3) {
+            tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 3 * BN + c0, v3);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v3[j] = 0u;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = __float_as_uint(__fadd_rn(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(v1[j])),
+                                             __fadd_rn(__uint_as_float(v2[j]), __uint_as_float(v3[j]))));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(v1[j])));
+        }
+      }
+      if (row < p.m) {
+        uint16_t* dst = p.y + row * p.n + n0 + c0;
+        const int64_t cols = p.n - (n0 + c0);
+        if (cols >= 32 && (p.n % 8) == 0) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[8 * q + 2 * j]), gamma));
+              const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[8 * q + 2 * j + 1]), gamma));
+              pk[j] = lo | (hi << 16);
+            }
+            reinterpret_cast<uint4*>(dst)[q] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        } else {
+          for (int j = 0; j < 32 && j < cols; ++j) dst[j] = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[j]), gamma));
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN * kPgAcc) : "memory");
+}
+
+}  // namespace nvfp4da

@@ -29,7 +29,7 @@ EXPORTED = (
     "nvfp4da_decoder_attention_forward_path", "nvfp4da_forward_step_supported", "nvfp4da_forward_sync_status",
     "nvfp4da_debug_wait_timeout", "nvfp4da_qkv_rope_append_shard",
     "nvfp4da_gqa_attention_partials_workspace_size", "nvfp4da_gqa_attention_partials",
-    "nvfp4da_attention_combine",
+    "nvfp4da_attention_combine", "nvfp4da_w4a16_gemm",
 )
 
 PATH_AUTO, PATH_CHAIN, PATH_STEP = 0, 1, 2
@@ -101,6 +101,7 @@ def load() -> C.CDLL:
         "nvfp4da_gqa_attention_partials": (C.c_int, [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, vp,
                                                      i64, vp, sz, vp]),
         "nvfp4da_attention_combine": (C.c_int, [vp, C.c_int, i64, i64, vp, vp]),
+        "nvfp4da_w4a16_gemm": (C.c_int, [vp, i64, C.POINTER(Weight), vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -139,6 +140,17 @@ def w4a16_linear(x: torch.Tensor, w, y: torch.Tensor | None = None, stream=None)
         y = torch.empty((*x.shape[:-1], rows), dtype=torch.bfloat16, device=x.device)
     wt = weight(w)
     _check(load().nvfp4da_w4a16_linear(_p(x), m, C.byref(wt), _p(y), _stream(stream)))
+    return y
+
+
+def w4a16_gemm(x: torch.Tensor, w, y: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """The projection forced onto the tcgen05 tensor-core GEMM."""
+    rows, cols = (int(v) for v in w.logical_shape)
+    m = x.numel() // cols
+    if y is None:
+        y = torch.empty((*x.shape[:-1], rows), dtype=torch.bfloat16, device=x.device)
+    wt = weight(w)
+    _check(load().nvfp4da_w4a16_gemm(_p(x), m, C.byref(wt), _p(y), _stream(stream)))
     return y
 
 

@@ -87,6 +87,12 @@ int nvfp4da_apply_rope(const uint16_t* x, uint16_t* out, int64_t batch, int64_t 
  * (include/w4a16_grouped.h:15-20): y[M, N] = BF16(x[M, K] @ W_hat^T). */
 int nvfp4da_w4a16_linear(const uint16_t* x, int64_t m, const nvfp4da_weight* w, uint16_t* y, void* stream);
 
+/* The same projection forced onto the tcgen05 tensor-core GEMM (BF16
+ * operands from the in-shared-memory dequantization, FP32 accumulator in
+ * tensor memory).  nvfp4da_w4a16_linear takes it by itself for M >= 64.  Needs
+ * K % 256 == 0; NVFP4DA_ERR_UNSUPPORTED otherwise.  Replaces
+ * launch_w4a16_linear_cuda (include/w4a16.h:15-20) for prefill-sized M. */
+int nvfp4da_w4a16_gemm(const uint16_t* x, int64_t m, const nvfp4da_weight* w, uint16_t* y, void* stream);
 /* Replaces launch_kv_cache_append_cuda (include/kv_cache.h:18-25; op
  * src/bindings.cpp:784-884): cache[b, h, P_b + t, :] = new[b, t, h, :] for K and V.
  * P_b = past_lengths[b] when past_lengths (device int64 [B]) is not NULL,
