@@ -160,6 +160,7 @@ int check_weight(const nvfp4da_weight* w, const char* name) {
 bool gemm_tc_supported(const uint16_t* x, int64_t m, const nvfp4da_weight& w, const uint16_t* y);
 int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s);
 constexpr int64_t kGemmMinMDecl = 64;  // at and above this M the tensor-core GEMM replaces the GEMV
+constexpr int64_t kPrefillMinM = 128;  // at and above this M the forward takes the modular chain
 
 // ---------------------------------------------------------------- GEMV plan
 struct GemvPlan {
@@ -549,7 +550,10 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   const int64_t maxp = a->past_lengths ? a->max_past_length : a->past_length;
   if (!plan_attention(a->batch, a->tokens, hq, a->kv_heads, a->head_dim, maxp, L.attn))
     return fail(NVFP4DA_ERR_UNSUPPORTED, "head_dim %lld is not supported", static_cast<long long>(a->head_dim));
-  L.fused = plan_qkv(m, a->hidden, a->head_dim, L.qkv);
+  // Prefill-sized M: the modular chain, whose projections run on the
+  // tensor-core GEMM; the fused front half re-decodes its weights for every 8
+  // activation rows.
+  L.fused = m < kPrefillMinM && plan_qkv(m, a->hidden, a->head_dim, L.qkv);
   const size_t act = align_up(static_cast<size_t>(m * a->hidden) * 2, 256);
   const size_t kvact = align_up(static_cast<size_t>(m * a->kv_heads * a->head_dim) * 2, 256);
   size_t off = 0;
@@ -1165,20 +1169,21 @@ int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* 
     if ((r = run_gemv(xn, m, a->v_weight, vp, s, false))) return r;
     if ((r = nvfp4da_rms_norm(qp, a->q_norm_weight, qn, m * hq, d, a->rms_eps, s))) return r;
     if ((r = nvfp4da_rms_norm(kp, a->k_norm_weight, kn, m * a->kv_heads, d, a->rms_eps, s))) return r;
-    if (a->past_lengths) {
-      // Per-sequence positions: RoPE one sequence at a time is not expressible
-      // without reading past_lengths on the host; the fused path covers it.
-      return fail(NVFP4DA_ERR_UNSUPPORTED, "per-sequence past_lengths need head_dim % 32 == 0");
-    }
-    if ((r = nvfp4da_apply_rope(qn, q_buf, a->batch, a->tokens, hq, d, a->past_length, a->rope_theta, s))) return r;
-    if ((r = nvfp4da_apply_rope(kn, kr, a->batch, a->tokens, a->kv_heads, d, a->past_length, a->rope_theta, s)))
-      return r;
+    auto rope = [&](const uint16_t* in, uint16_t* out, int64_t heads) {
+      const int64_t pairs = a->batch * a->tokens * heads * d / 2;
+      rope_kernel<<<static_cast<unsigned>(ceil_div(pairs, 256)), 256, 0, s>>>(
+          in, out, pairs, a->tokens, heads, d, a->past_length, a->rope_theta, a->past_lengths);
+      NVFP4DA_CHECK_LAUNCH("rope launch");
+      return NVFP4DA_OK;
+    };
+    if ((r = rope(qn, q_buf, hq))) return r;
+    if ((r = rope(kn, kr, a->kv_heads))) return r;
     if ((r = nvfp4da_kv_cache_append(a->k_cache, a->v_cache, kr, vp, a->batch, a->kv_heads, a->capacity, d,
-                                     a->tokens, a->past_length, nullptr, s)))
+                                     a->tokens, a->past_length, a->past_lengths, s)))
       return r;
     r = run_attention(q_buf, a->k_cache, a->v_cache, ctx_buf, a->batch, a->tokens, hq, a->kv_heads, a->capacity, d,
-                      a->past_length, nullptr, maxp, attn_ws, L.attn.partial_bytes + L.attn.counter_bytes, s, false,
-                      true);
+                      a->past_length, a->past_lengths, maxp, attn_ws, L.attn.partial_bytes + L.attn.counter_bytes, s,
+                      false, true);
     if (r) return r;
   }
   if ((r = run_gemv(ctx_buf, m, a->out_weight, a->output, s, L.fused))) return r;

@@ -66,15 +66,18 @@ __device__ __forceinline__ void rope_pair(float xe, float xo, float c, float s, 
   yo = f32_to_bf16_bits(__fadd_rn(__fmul_rn(xe, s), __fmul_rn(xo, c)));
 }
 
+// Positions P_b + t: P_b = past_lengths[b] when given (device int64 [B]),
+// else past_length.
 __global__ void rope_kernel(const uint16_t* x, uint16_t* out, int64_t total_pairs, int64_t tokens, int64_t heads,
-                            int64_t head_dim, int64_t past_length, float theta) {
+                            int64_t head_dim, int64_t past_length, float theta,
+                            const int64_t* past_lengths = nullptr) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total_pairs) return;
   const int64_t pairs = head_dim / 2;
   const int64_t row = i / pairs;  // ((b*T + t)*H + h)
   const int64_t m = i % pairs;
   const int64_t t = (row / heads) % tokens;
-  const int64_t pos = past_length + t;
+  const int64_t pos = (past_lengths ? past_lengths[row / heads / tokens] : past_length) + t;
   const int64_t off = row * head_dim + 2 * m;
   if (pos == 0) {
     out[off] = x[off];
