@@ -346,6 +346,71 @@ def run_gpu(args) -> None:
     _finish(world)
 
 
+def run_prefill(args) -> None:
+    """configs[4] (B=4, T=2048, P=0, C=4096): the prefill forward (modular chain
+    with tcgen05 GEMM projections); not the default workload.  Roofline on the
+    tensor-core GEMM (BF16 dense, measured cuBLAS peak)."""
+    world, rank, local = dist_setup()
+    import nvfp4da_capi as capi
+    import synthetic
+    from nvfp4_tensor import NVFP4Tensor
+
+    capi.load()
+    shape = synthetic.DecodeShape(batch=4, tokens=2048, hidden=3072, kv_heads=6, head_dim=128, capacity=4096,
+                                  past_lengths=(0,))
+    inp = synthetic.make_decode_inputs(shape, seed=0)
+    ws = {}
+    for k, w in inp.weights_fp32.items():
+        packed, scales, gamma = capi.quantize(w.cuda())
+        ws[k] = NVFP4Tensor(packed, scales, gamma, tuple(w.shape))
+    x = inp.x.cuda()
+    kc, vc = inp.k_cache.cuda(), inp.v_cache.cuda()
+    out = torch.empty_like(x)
+    fw = capi.Forward(x, inp.input_norm_weight.cuda(), ws["q"], ws["k"], ws["v"], inp.q_norm_weight.cuda(),
+                      inp.k_norm_weight.cuda(), ws["o"], kc, vc, out, past_length=0)
+    stream = torch.cuda.Stream()
+    m, h, kvw = 4 * 2048, 3072, 6 * 128
+    xin = torch.randn((m, h), device="cuda").to(torch.bfloat16)
+    y = torch.empty((m, h), dtype=torch.bfloat16, device="cuda")
+    yk = torch.empty((m, kvw), dtype=torch.bfloat16, device="cuda")
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            fw.run(stream)
+            capi.w4a16_gemm(xin, ws["q"], y, stream)
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 20))
+    ms = timed_graph([lambda: fw.run(stream)], steps, stream) / steps
+    gemm_ms = {
+        "q_or_o": timed_graph([lambda: capi.w4a16_gemm(xin, ws["q"], y, stream)], steps, stream) / steps,
+        "k_or_v": timed_graph([lambda: capi.w4a16_gemm(xin, ws["k"], yk, stream)], steps, stream) / steps,
+    }
+    fl = {"q_or_o": 2.0 * m * h * h, "k_or_v": 2.0 * m * kvw * h}
+    tflops = {n: fl[n] / (gemm_ms[n] * 1e-3) / 1e12 for n in fl}
+    try:
+        peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+        src = "measured (MEASURED_PEAKS.json bf16_tflops)"
+    except Exception:
+        peak, src = 1590.0, "fallback 1.59 PFLOP/s"
+    step_flops = 2.0 * m * h * (h + 2 * kvw + h) + 4 * 24 * 2 * 2048 * 2048 * 128  # projections + causal attention
+    if rank == 0:
+        print(json.dumps({
+            "metric": "prefill tokens/s (configs[4])", "value": round(m / (ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; configs[4] distributions, random-init NVFP4 weights)",
+            "config": {"workload": "configs[4] prefill: B=4 T=2048 H=3072 Hq=24 Hkv=6 D=128 P=0 C=4096",
+                       "global_batch": 4, "seq_len": 2048, "parallelism": "single"},
+            "roofline": {"bound": "tensor", "kernel": "w4a16_gemm_tc_kernel (Q/O projection, M=8192 N=3072 K=3072)",
+                         "achieved": round(tflops["q_or_o"], 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops["q_or_o"] / peak, 4), "peak_source": src, "traffic": None},
+            "gemm_ms": {n: round(v, 4) for n, v in gemm_ms.items()},
+            "gemm_tflops": {n: round(v, 1) for n, v in tflops.items()},
+            "step_tflops": round(step_flops / (ms * 1e-3) / 1e12, 1),
+            "gpu_launches": None,
+        }), flush=True)
+    _finish(world)
+
+
 def run_e2e(args, reps, dac, stream, world) -> dict:
     """Same metric through cuda_decoder_attention_forward_ with pinned host
     input copied in and the output copied out every step (inside the timing)."""
@@ -462,9 +527,13 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
+                    help="decode = configs[0] (the metric's workload); prefill = configs[4], reported separately")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_gpu(args)
 

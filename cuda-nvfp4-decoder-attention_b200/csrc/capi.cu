@@ -17,6 +17,7 @@
 
 #include "../../include/nvfp4_decoder_attention.h"
 #include "attention.cuh"
+#include "attention_prefill.cuh"
 #include "elementwise.cuh"
 #include "gemv_kernel.cuh"
 #include "prefill_gemm.cuh"
@@ -161,6 +162,7 @@ bool gemm_tc_supported(const uint16_t* x, int64_t m, const nvfp4da_weight& w, co
 int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s);
 constexpr int64_t kGemmMinMDecl = 64;  // at and above this M the tensor-core GEMM replaces the GEMV
 constexpr int64_t kPrefillMinM = 128;  // at and above this M the forward takes the modular chain
+constexpr int64_t kPrefillAttnMinT = 64;  // at and above this T attention runs on the tensor cores
 
 // ---------------------------------------------------------------- GEMV plan
 struct GemvPlan {
@@ -249,7 +251,7 @@ int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y,
 }
 
 // ---------------------------------------------------------------- tensor-core GEMM (prefill-sized M)
-constexpr int kPgBN = 128;
+constexpr int kPgBN = 128;  // x kPgAcc accumulators = 512 tensor-memory columns
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -419,6 +421,19 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
                   int64_t past_length, const int64_t* past_lengths, int64_t max_past, void* ws, size_t ws_bytes,
                   cudaStream_t s, bool pdl, bool clear_counters, int64_t pos_offset = 0,
                   float* out_partial = nullptr) {
+  // Prefill-sized T: the tensor-core kernel (one CTA per 64 query tokens).
+  if (tokens >= kPrefillAttnMinT && head_dim == kPaD && !out_partial && pos_offset == 0 && aligned(q, 16) &&
+      aligned(kc, 16) && aligned(vc, 16) && aligned(ctx, 4) && batch <= 65535 && q_heads <= 65535) {
+    PrefillAttnParams pp{q, kc, vc, ctx, batch, tokens, q_heads, kv_heads, capacity, past_length, past_lengths,
+                         static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)))};
+    cudaError_t e = ensure_smem(attn_prefill_kernel, kPaSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill attention shared-memory opt-in");
+    const dim3 grid(static_cast<unsigned>(ceil_div(tokens, kPaRows)), static_cast<unsigned>(q_heads),
+                    static_cast<unsigned>(batch));
+    attn_prefill_kernel<<<grid, kPaThreads, kPaSmem, s>>>(pp);
+    NVFP4DA_CHECK_LAUNCH("prefill attention launch");
+    return NVFP4DA_OK;
+  }
   AttnPlan pl;
   if (!plan_attention(batch, tokens, q_heads, kv_heads, head_dim, max_past, pl))
     return fail(NVFP4DA_ERR_UNSUPPORTED, "head_dim %lld is not supported (need head_dim <= 256 and divisible by "

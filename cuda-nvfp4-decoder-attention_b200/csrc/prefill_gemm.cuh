@@ -113,6 +113,38 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// Sum of accumulators [a, a + n) of 16 columns, pairwise (n a power of two);
+// accumulators at or past `used` (never written) count as zero.
+template <int N>
+__device__ __forceinline__ void tmem_sum_x16(uint32_t base, uint32_t stride, int a, int used, float (&out)[16]) {
+  if constexpr (N == 1) {
+    if (a < used) {
+      tmem_ld_32x32b_x16(base + a * stride, out);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] = 0.0f;
+    }
+  } else {
+    float r[16];
+    tmem_sum_x16<N / 2>(base, stride, a, used, out);
+    tmem_sum_x16<N / 2>(base, stride, a + N / 2, used, r);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) out[j] = __fadd_rn(out[j], r[j]);
+  }
+}
+
 // Exact f16x2 -> bf16x2 for the decoded weights (at most 6 significant bits).
 __device__ __forceinline__ uint32_t f16x2_to_bf16x2_exact(uint32_t h) {
   float lo, hi;
@@ -228,29 +260,15 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     const int64_t row = m0 + warp * 32 + lane;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
+      // The accumulators that received K steps, added pairwise: ((a0 + a1) + (a2 + a3)) + ...
       uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-      // Sum the accumulators that received K steps: ((a0 + a1) + (a2 + a3)).
-      if (nk > 1) {
-        uint32_t v1[32];
-        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + BN + c0, v1);
-        if (nk > 2) {
-          uint32_t v2[32], v3[32];
-          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 2 * BN + c0, v2);
-          if (nk > 3) {
-            tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 3 * BN + c0, v3);
-          } else {
+      const uint32_t base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v3[j] = 0u;
-          }
+      for (int half = 0; half < 2; ++half) {
+        float f[16];
+        tmem_sum_x16<kPgAcc>(base + c0 + 16 * half, BN, 0, nk, f);
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = __float_as_uint(__fadd_rn(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(v1[j])),
-                                             __fadd_rn(__uint_as_float(v2[j]), __uint_as_float(v3[j]))));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(v1[j])));
-        }
+        for (int j = 0; j < 16; ++j) v[16 * half + j] = __float_as_uint(f[j]);
       }
       if (row < p.m) {
         uint16_t* dst = p.y + row * p.n + n0 + c0;
