@@ -311,6 +311,9 @@ void expect_forward(const ForwardTensors& f) {
   expect_rank4(f.vc, "v_cache");
   TORCH_CHECK(f.vc.sizes() == f.kc.sizes(), "v_cache must have the same shape as k_cache");
   for (const Tensor* t : {&f.g_in, &f.g_q, &f.g_k}) expect(*t, "norm weight", at::kBFloat16);
+  TORCH_CHECK(f.g_in.dim() == 1 && f.g_in.size(0) == f.x.size(2), "input_norm_weight must have shape [H]");
+  TORCH_CHECK(f.g_q.dim() == 1 && f.g_q.size(0) == f.kc.size(3), "q_norm_weight must have shape [D]");
+  TORCH_CHECK(f.g_k.dim() == 1 && f.g_k.size(0) == f.kc.size(3), "k_norm_weight must have shape [D]");
   const Tensor* w[4][3] = {{&f.qp, &f.qs, &f.qg}, {&f.kp, &f.ks, &f.kg}, {&f.vp, &f.vs, &f.vg}, {&f.op, &f.os, &f.og}};
   for (auto& t : w) {
     expect_packed(*t[0]);

@@ -17,7 +17,7 @@ import math
 import torch
 
 import cuda_primitives
-from nvfp4_tensor import is_nvfp4_tensor
+from nvfp4_tensor import NVFP4Tensor, is_nvfp4_tensor
 
 _ops = torch.ops.cuda_nvfp4_decoder_attention
 _INT64_MAX = 2**63 - 1
@@ -141,6 +141,23 @@ def cuda_decoder_attention_forward_(x, input_norm_weight, q_weight, k_weight, v_
         raise TypeError("past_length must be an integer")
     if past_length < 0:
         raise ValueError(f"past_length must be nonnegative, got {past_length}")
+    # Fast path: the operator itself checks every tensor property the Python
+    # validation below checks (dtype, rank, contiguity, device, shapes,
+    # capacity, eps/theta) before any launch.  NVFP4Tensor weights were
+    # validated when constructed.  Only when the operator rejects the call is
+    # the Python validation run, to raise the reference's exception type and
+    # message.
+    ws4 = (q_weight, k_weight, v_weight, out_weight)
+    if all(type(w) is NVFP4Tensor for w in ws4) and type(rms_eps) is float and type(rope_theta) in (float, int):
+        (qp, qs, qg), (kp, ks, kg), (vp, vs, vg), (op, os_, og) = _flat(ws4)
+        try:
+            return _ops.cuda_decoder_attention_forward_(x, input_norm_weight, qp, qs, qg, kp, ks, kg, vp, vs, vg,
+                                                        q_norm_weight, k_norm_weight, op, os_, og, k_cache, v_cache,
+                                                        past_length, rms_eps, float(rope_theta))
+        except Exception:
+            _validate(x, input_norm_weight, q_weight, k_weight, v_weight, q_norm_weight, k_norm_weight, out_weight,
+                      k_cache, v_cache, past_length, rms_eps, rope_theta)
+            raise
     x, g_in, g_q, g_k, kc, vc, ws, eps, theta = _validate(
         x, input_norm_weight, q_weight, k_weight, v_weight, q_norm_weight, k_norm_weight, out_weight, k_cache,
         v_cache, past_length, rms_eps, rope_theta)

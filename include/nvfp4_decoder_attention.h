@@ -160,7 +160,8 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* wo
 
 /* Forward with an explicit kernel path.  NVFP4DA_PATH_AUTO (what
  * nvfp4da_decoder_attention_forward uses) takes the faster path for the call
- * as measured on B200 (currently the three-kernel chain everywhere);
+ * as measured on B200 (the one-kernel step where it applies: same device
+ * time as the chain, one launch instead of three);
  * NVFP4DA_PATH_CHAIN always takes the chain; NVFP4DA_PATH_STEP takes the
  * one-kernel decode step or fails with NVFP4DA_ERR_UNSUPPORTED.  Same results within the numerics policy (the
  * FP32 summation order of the projections and of the attention splits
