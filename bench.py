@@ -310,6 +310,27 @@ def run_gpu(args) -> None:
     qkv_gbs = nbytes["qkv"] / (per_launch_us["qkv"] * 1e-6) / 1e9
     step_gbs = nbytes["step"] / (ms_per_step * 1e-3) / 1e9
 
+    # Dominant kernel: the one-kernel step (the default path, one launch per
+    # step) when it covers the shape, else the chain's fused QKV kernel.
+    if "step" in path_ms:
+        step_us = path_ms["step"] * 1e3 / (reps_k * n_rep)
+        gbs = nbytes["step"] / (step_us * 1e-6) / 1e9
+        roofline = {"bound": "hbm", "kernel": "decode_step_kernel (the whole step, one cooperative launch)",
+                    "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                    "peak_source": peak_src, "traffic": ncu_traffic("decode_step"),
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                      "(profiles/decode_step_canonical.md)",
+                    "bytes_per_launch": nbytes["step"]}
+    else:
+        roofline = {"bound": "hbm", "kernel": "qkv_fused (input norm + W4A16 QKV + head norm + RoPE + append)",
+                    "achieved": round(qkv_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(qkv_gbs / peak, 4),
+                    "peak_source": peak_src, "traffic": ncu_traffic("qkv_fused"),
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                      "(profiles/qkv_fused_canonical.md)",
+                    "bytes_per_launch": nbytes["qkv"]}
+    roofline.update({"step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
+                     "step_bytes": nbytes["step"]})
+
     # ---- end to end through the drop-in Python API with host buffers
     e2e = run_e2e(args, reps, decoder_attention_cuda, stream, world)
 
@@ -326,15 +347,7 @@ def run_gpu(args) -> None:
                    "l2": f"inputs larger than L2: {n_rep} rotating weight+cache replicas "
                          f"({n_rep * replica_bytes / 2**20:.0f} MiB > 2 x 126 MB L2)",
                    "timing": f"CUDA graph of {n_rep} steps replayed, CUDA events"},
-        "roofline": {"bound": "hbm", "kernel": "qkv_fused (input norm + W4A16 QKV + head norm + RoPE + append)",
-                     "achieved": round(qkv_gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(qkv_gbs / peak, 4), "peak_source": peak_src,
-                     "traffic": ncu_traffic("qkv_fused"),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                                       "(profiles/qkv_fused_canonical.md)",
-                     "bytes_per_launch": nbytes["qkv"],
-                     "step_achieved": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
-                     "step_bytes": nbytes["step"]},
+        "roofline": roofline,
         "kernels": kernels,
         "paths_us_per_step": {n: round(v * 1e3 / (reps_k * n_rep), 3) for n, v in path_ms.items()},
         "e2e": e2e,
