@@ -10,13 +10,13 @@
 // operands, FP32 accumulators in tensor memory), K in steps of 64:
 //  * x tile [128 rows x 64 k] by TMA with 128-byte swizzle (the canonical
 //    K-major SW128 operand layout), the packed weight tile [BN x 32 bytes] and,
-//    every 4 steps, the scale tile [BN x 16 bytes] by TMA, double-buffered on
+//    the scale tile [BN x 16 bytes] by TMA, kPgStages stages in flight on
 //    mbarriers;
 //  * the 128 threads decode the weight tile (one row each: E2M1 -> f16 by the
 //    hardware conversion, times the UE4M3 scale, -> BF16, all exact) into the
 //    SW128 K-major layout in shared memory;
 //  * one thread issues the four K=16 MMAs of the step and commits them to the
-//    stage's mbarrier, which frees the stage for the loads two steps ahead;
+//    stage's mbarrier; a stage is refilled once its MMAs are done;
 //  * epilogue: each warp reads its 32 accumulator lanes (rows) with
 //    tcgen05.ld, scales by gamma and stores BF16.
 // Every wait is bounded; on expiry the kernel records kErrBarrierTimeout,
@@ -44,20 +44,24 @@ struct PgParams {
   unsigned* err;
 };
 
+// Load stages in flight (x tile, packed weights, scales); the decoded weight
+// tile is double-buffered.
+constexpr int kPgStages = 6;
+
 // Shared-memory layout of one CTA (byte offsets from a 1024-aligned base).
 template <int BN>
 struct PgLayout {
   static constexpr uint32_t kA = kPgBM * kPgBK * 2;  // 16 KB per stage
-  static constexpr uint32_t kB = BN * kPgBK * 2;     // decoded weight tile per stage
+  static constexpr uint32_t kB = BN * kPgBK * 2;     // decoded weight tile per buffer
   static constexpr uint32_t kW = BN * kPgBK / 2;     // packed weight tile per stage
-  static constexpr uint32_t kS = BN * 16;            // scales of 4 steps
+  static constexpr uint32_t kS = BN * 16;            // scale bytes of 4 steps per stage
   __host__ __device__ static constexpr uint32_t a(int s) { return s * kA; }
-  __host__ __device__ static constexpr uint32_t b(int s) { return 2 * kA + s * kB; }
-  __host__ __device__ static constexpr uint32_t w(int s) { return 2 * kA + 2 * kB + s * kW; }
-  __host__ __device__ static constexpr uint32_t sc(int s) { return 2 * kA + 2 * kB + 2 * kW + s * kS; }
+  __host__ __device__ static constexpr uint32_t b(int d) { return kPgStages * kA + d * kB; }
+  __host__ __device__ static constexpr uint32_t w(int s) { return kPgStages * kA + 2 * kB + s * kW; }
+  __host__ __device__ static constexpr uint32_t sc(int s) { return kPgStages * (kA + kW) + 2 * kB + s * kS; }
   // + 1024 alignment slack; at least 116 KB so that one CTA (which holds all
   // 512 tensor-memory columns) runs per SM.
-  __host__ __device__ static constexpr uint32_t used() { return 2 * kA + 2 * kB + 2 * kW + 2 * kS + 1024; }
+  __host__ __device__ static constexpr uint32_t used() { return kPgStages * (kA + kW + kS) + 2 * kB + 1024; }
   __host__ __device__ static constexpr uint32_t total() { return used() > 116u * 1024 ? used() : 116u * 1024; }
 };
 
@@ -164,7 +168,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   using L = PgLayout<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_load[2], bar_mma[2];
+  __shared__ uint64_t bar_load[kPgStages], bar_mma[kPgStages];
   __shared__ uint32_t tmem_base;
   __shared__ unsigned s_bad;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -178,7 +182,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kPgStages; ++s) {
       mbar_init(&bar_load[s], 1);
       mbar_init(&bar_mma[s], 1);
     }
@@ -190,25 +194,29 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base;
 
+  // Step kt uses load stage kt % kPgStages and decoded buffer kt & 1.  The
+  // tensor cores finish MMAs in order, so once the MMAs of step kt - 2 are
+  // done both decoded buffer kt & 1 and load stage (kt - 2) % kPgStages are
+  // free: the loads run kPgStages - 2 steps ahead of the decode.
   auto issue = [&](int kt) {
-    const int st = kt & 1;
-    const bool with_scales = (kt & 3) == 0;
-    mbar_arrive_expect_tx(&bar_load[st], L::kA + L::kW + (with_scales ? L::kS : 0u));
+    const int st = kt % kPgStages;
+    mbar_arrive_expect_tx(&bar_load[st], L::kA + L::kW + L::kS);
     tma_load_2d(smem + L::a(st), &tm_x, kt * kPgBK, m0, &bar_load[st]);
     tma_load_2d(smem + L::w(st), &tm_w, kt * (kPgBK / 2), n0, &bar_load[st]);
-    if (with_scales) tma_load_2d(smem + L::sc((kt >> 2) & 1), &tm_s, kt * (kPgBK / 16), n0, &bar_load[st]);
+    tma_load_2d(smem + L::sc(st), &tm_s, (kt >> 2) * 16, n0, &bar_load[st]);
   };
-  if (tid == 0) issue(0);
+  if (tid == 0)
+    for (int j = 0; j < kPgStages && j < nk; ++j) issue(j);
 
   constexpr uint32_t kIdesc = umma_idesc_bf16(kPgBM, BN);
   for (int kt = 0; kt < nk; ++kt) {
-    const int st = kt & 1;
-    if (kt + 1 < nk) {
-      // Stage (kt + 1) & 1 was last read by the MMAs of step kt - 1.
-      if (kt >= 1 && !mbar_wait_bounded(&bar_mma[(kt + 1) & 1], ((kt - 1) >> 1) & 1, p.err)) s_bad = 1u;
-      if (tid == 0) issue(kt + 1);
+    const int st = kt % kPgStages, db = kt & 1;
+    if (kt >= 2) {
+      const int done = kt - 2;
+      if (!mbar_wait_bounded(&bar_mma[done % kPgStages], (done / kPgStages) & 1, p.err)) s_bad = 1u;
+      if (tid == 0 && done + kPgStages < nk) issue(done + kPgStages);
     }
-    if (!mbar_wait_bounded(&bar_load[st], (kt >> 1) & 1, p.err)) s_bad = 1u;
+    if (!mbar_wait_bounded(&bar_load[st], (kt / kPgStages) & 1, p.err)) s_bad = 1u;
     __syncthreads();
     if (s_bad) break;
     // ---- decode this thread's weight row for k-step kt into the SW128 layout
@@ -217,8 +225,8 @@ __global__ void __launch_bounds__(kPgThreads, 1)
       const uint4* wp = reinterpret_cast<const uint4*>(smem + L::w(st) + row * (kPgBK / 2));
       const uint4 w01 = wp[0], w23 = wp[1];
       const uint32_t words[8] = {w01.x, w01.y, w01.z, w01.w, w23.x, w23.y, w23.z, w23.w};
-      const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(smem + L::sc((kt >> 2) & 1) + row * 16 + (kt & 3) * 4);
-      uint8_t* brow = smem + L::b(st) + row * 128;
+      const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(smem + L::sc(st) + row * 16 + (kt & 3) * 4);
+      uint8_t* brow = smem + L::b(db) + row * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // chunk c = 8 k = word c
         uint32_t beta;
@@ -242,7 +250,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     if (tid == 0) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint64_t ad = umma_desc_sw128(smem_u32(smem + L::a(st)));
-      const uint64_t bd = umma_desc_sw128(smem_u32(smem + L::b(st)));
+      const uint64_t bd = umma_desc_sw128(smem_u32(smem + L::b(db)));
       const uint32_t acc = tmem + static_cast<uint32_t>((kt % kPgAcc) * BN);
 #pragma unroll
       for (int kk = 0; kk < kPgBK / 16; ++kk)  // +32 bytes of K per MMA inside the swizzle atom
@@ -252,7 +260,9 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   }
 
   // ---- epilogue: accumulator lanes = tile rows
-  if (!s_bad && nk > 0 && !mbar_wait_bounded(&bar_mma[(nk - 1) & 1], ((nk - 1) >> 1) & 1, p.err)) s_bad = 1u;
+  if (!s_bad && nk > 0 &&
+      !mbar_wait_bounded(&bar_mma[(nk - 1) % kPgStages], ((nk - 1) / kPgStages) & 1, p.err))
+    s_bad = 1u;
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (!s_bad) {
