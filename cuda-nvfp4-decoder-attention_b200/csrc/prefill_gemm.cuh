@@ -7,18 +7,21 @@
 // in the FP32 accumulator, and gamma is applied once in the epilogue.
 //
 // One CTA computes a 128 x BN tile of y with tcgen05.mma (kind::f16, BF16
-// operands, FP32 accumulators in tensor memory), K in steps of 64:
-//  * x tile [128 rows x 64 k] by TMA with 128-byte swizzle (the canonical
-//    K-major SW128 operand layout), the packed weight tile [BN x 32 bytes] and,
-//    the scale tile [BN x 16 bytes] by TMA, kPgStages stages in flight on
-//    mbarriers;
-//  * the 128 threads decode the weight tile (one row each: E2M1 -> f16 by the
-//    hardware conversion, times the UE4M3 scale, -> BF16, all exact) into the
-//    SW128 K-major layout in shared memory;
-//  * one thread issues the four K=16 MMAs of the step and commits them to the
-//    stage's mbarrier; a stage is refilled once its MMAs are done;
-//  * epilogue: each warp reads its 32 accumulator lanes (rows) with
-//    tcgen05.ld, scales by gamma and stores BF16.
+// operands, FP32 accumulators in tensor memory), K in steps of 64, as a
+// warp-specialised pipeline on mbarriers:
+//  * warp 0 (one lane) streams, kPgStages steps ahead, the x tile [128 rows x
+//    64 k] by TMA with 128-byte swizzle (the canonical K-major SW128 operand
+//    layout), the packed weight tile [BN x 32 bytes] and the scale tile
+//    [BN x 16 bytes];
+//  * warps 2-9 decode the weight tile (two threads per row, 32 k each) into
+//    one of kPgDec BF16 buffers in the SW128 K-major layout: E2M1 -> BF16 by
+//    byte permutes from two 8-entry tables (sign from the nibble's top bit),
+//    times the UE4M3 block scale in BF16, all exact;
+//  * warp 1 (one lane) issues the four K=16 MMAs of a step once its x tile and
+//    decoded buffer are ready, and commits them to the barriers that free the
+//    load stage and the decoded buffer;
+//  * epilogue: warps 2-5 (one per 32-lane quarter of tensor memory) read the
+//    accumulators with tcgen05.ld, scale by gamma and store BF16.
 // Every wait is bounded; on expiry the kernel records kErrBarrierTimeout,
 // skips the remaining work, and still frees its tensor memory.
 #pragma once
@@ -31,7 +34,8 @@ namespace nvfp4da {
 
 constexpr int kPgBM = 128;
 constexpr int kPgBK = 64;
-constexpr int kPgThreads = 128;
+constexpr int kPgThreads = 320;  // TMA warp, MMA warp, 8 decode warps
+constexpr int kPgDecodeWarps = 8;
 // K steps go round-robin to kPgAcc accumulators (TMEM column blocks) that the
 // epilogue adds in FP32: shorter accumulation chains keep the tensor cores'
 // internal rounding within one BF16 step of the correctly rounded sum.
@@ -44,9 +48,10 @@ struct PgParams {
   unsigned* err;
 };
 
-// Load stages in flight (x tile, packed weights, scales); the decoded weight
-// tile is double-buffered.
+// Load stages in flight (x tile, packed weights, scales) and decoded weight
+// buffers.
 constexpr int kPgStages = 6;
+constexpr int kPgDec = 3;
 
 // Shared-memory layout of one CTA (byte offsets from a 1024-aligned base).
 template <int BN>
@@ -57,12 +62,12 @@ struct PgLayout {
   static constexpr uint32_t kS = BN * 16;            // scale bytes of 4 steps per stage
   __host__ __device__ static constexpr uint32_t a(int s) { return s * kA; }
   __host__ __device__ static constexpr uint32_t b(int d) { return kPgStages * kA + d * kB; }
-  __host__ __device__ static constexpr uint32_t w(int s) { return kPgStages * kA + 2 * kB + s * kW; }
-  __host__ __device__ static constexpr uint32_t sc(int s) { return kPgStages * (kA + kW) + 2 * kB + s * kS; }
-  // + 1024 alignment slack; at least 116 KB so that one CTA (which holds all
-  // 512 tensor-memory columns) runs per SM.
-  __host__ __device__ static constexpr uint32_t used() { return kPgStages * (kA + kW + kS) + 2 * kB + 1024; }
-  __host__ __device__ static constexpr uint32_t total() { return used() > 116u * 1024 ? used() : 116u * 1024; }
+  __host__ __device__ static constexpr uint32_t w(int s) { return kPgStages * kA + kPgDec * kB + s * kW; }
+  __host__ __device__ static constexpr uint32_t sc(int s) { return kPgStages * (kA + kW) + kPgDec * kB + s * kS; }
+  // + 1024 alignment slack.  One CTA per SM: it holds all 512 tensor-memory
+  // columns.
+  __host__ __device__ static constexpr uint32_t total() { return kPgStages * (kA + kW + kS) + kPgDec * kB + 1024; }
+  static_assert(kPgStages * (kA + kW + kS) + kPgDec * kB + 1024 <= 227u * 1024, "shared memory per CTA");
 };
 
 // ---------------------------------------------------------------- tcgen05 / TMA primitives
@@ -149,6 +154,42 @@ __device__ __forceinline__ void tmem_sum_x16(uint32_t base, uint32_t stride, int
   }
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Eight E2M1 nibbles (nibble i = element i, low nibble first) -> four BF16x2,
+// exact, with integer byte permutes only.  The magnitude code (e1 e0 m) picks
+// the low and high byte of the BF16 value from two 8-entry tables:
+//   code      0    1    2    3    4    5    6    7
+//   value     0   0.5   1   1.5   2    3    4    6
+//   BF16   0000 3F00 3F80 3FC0 4000 4040 4080 40C0
+// and the nibble's sign bit becomes bit 15 of its BF16 half.
+__device__ __forceinline__ void e2m1x8_to_bf16x2x4(uint32_t w, uint32_t (&o)[4]) {
+  const uint32_t m = w & 0x77777777u;
+  const uint32_t lo0 = __byte_perm(0xC0800000u, 0xC0804000u, m);
+  const uint32_t hi0 = __byte_perm(0x3F3F3F00u, 0x40404040u, m);
+  const uint32_t lo1 = __byte_perm(0xC0800000u, 0xC0804000u, m >> 16);
+  const uint32_t hi1 = __byte_perm(0x3F3F3F00u, 0x40404040u, m >> 16);
+  const uint32_t mag[4] = {__byte_perm(lo0, hi0, 0x5140), __byte_perm(lo0, hi0, 0x7362),
+                           __byte_perm(lo1, hi1, 0x5140), __byte_perm(lo1, hi1, 0x7362)};
+  // Byte j of w holds the signs of elements 2j (bit 3) and 2j+1 (bit 7):
+  // byte j of (w << 4) into result byte 1 puts the first at bit 15, byte j of
+  // w into result byte 3 puts the second at bit 31.
+  const uint32_t w4 = w << 4;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t sg = __byte_perm(w4, w, static_cast<uint32_t>(((4 + j) << 12) | (j << 4)));
+    o[j] = mag[j] | (sg & 0x80008000u);
+  }
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // Exact f16x2 -> bf16x2 for the decoded weights (at most 6 significant bits).
 __device__ __forceinline__ uint32_t f16x2_to_bf16x2_exact(uint32_t h) {
   float lo, hi;
@@ -165,17 +206,20 @@ template <int BN>
 __global__ void __launch_bounds__(kPgThreads, 1)
     w4a16_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                          const __grid_constant__ CUtensorMap tm_s, PgParams p) {
+  static_assert(BN == 128, "two decode threads per weight row: 8 warps cover 128 rows");
   using L = PgLayout<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar_load[kPgStages], bar_mma[kPgStages];
+  // full: TMA bytes landed; empty: the step's MMAs are done with the stage;
+  // dfull: all decode warps wrote the buffer; dempty: its MMAs are done.
+  __shared__ uint64_t bar_full[kPgStages], bar_empty[kPgStages], bar_dfull[kPgDec], bar_dempty[kPgDec], bar_acc;
   __shared__ uint32_t tmem_base;
-  __shared__ unsigned s_bad;
+  __shared__ volatile unsigned s_bad;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m0 = blockIdx.y * kPgBM, n0 = blockIdx.x * BN;
   const int nk = static_cast<int>(p.k / kPgBK);
 
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                  "r"(BN * kPgAcc)
                  : "memory");
@@ -183,9 +227,14 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   }
   if (tid == 0) {
     for (int s = 0; s < kPgStages; ++s) {
-      mbar_init(&bar_load[s], 1);
-      mbar_init(&bar_mma[s], 1);
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
     }
+    for (int d = 0; d < kPgDec; ++d) {
+      mbar_init(&bar_dfull[d], kPgDecodeWarps);
+      mbar_init(&bar_dempty[d], 1);
+    }
+    mbar_init(&bar_acc, 1);
     fence_mbar_init();
     s_bad = 0u;
   }
@@ -194,116 +243,131 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base;
 
-  // Step kt uses load stage kt % kPgStages and decoded buffer kt & 1.  The
-  // tensor cores finish MMAs in order, so once the MMAs of step kt - 2 are
-  // done both decoded buffer kt & 1 and load stage (kt - 2) % kPgStages are
-  // free: the loads run kPgStages - 2 steps ahead of the decode.
-  auto issue = [&](int kt) {
-    const int st = kt % kPgStages;
-    mbar_arrive_expect_tx(&bar_load[st], L::kA + L::kW + L::kS);
-    tma_load_2d(smem + L::a(st), &tm_x, kt * kPgBK, m0, &bar_load[st]);
-    tma_load_2d(smem + L::w(st), &tm_w, kt * (kPgBK / 2), n0, &bar_load[st]);
-    tma_load_2d(smem + L::sc(st), &tm_s, (kt >> 2) * 16, n0, &bar_load[st]);
-  };
-  if (tid == 0)
-    for (int j = 0; j < kPgStages && j < nk; ++j) issue(j);
-
-  constexpr uint32_t kIdesc = umma_idesc_bf16(kPgBM, BN);
-  for (int kt = 0; kt < nk; ++kt) {
-    const int st = kt % kPgStages, db = kt & 1;
-    if (kt >= 2) {
-      const int done = kt - 2;
-      if (!mbar_wait_bounded(&bar_mma[done % kPgStages], (done / kPgStages) & 1, p.err)) s_bad = 1u;
-      if (tid == 0 && done + kPgStages < nk) issue(done + kPgStages);
+  if (warp == 0) {
+    // ---- producer: stage kt % kPgStages is refilled once the MMAs of step
+    // kt - kPgStages are done.
+    if (lane == 0) {
+      for (int kt = 0; kt < nk && !s_bad; ++kt) {
+        const int st = kt % kPgStages;
+        if (kt >= kPgStages &&
+            !mbar_wait_bounded(&bar_empty[st], ((kt / kPgStages) - 1) & 1, p.err)) {
+          s_bad = 1u;
+          break;
+        }
+        mbar_arrive_expect_tx(&bar_full[st], L::kA + L::kW + L::kS);
+        tma_load_2d(smem + L::a(st), &tm_x, kt * kPgBK, m0, &bar_full[st]);
+        tma_load_2d(smem + L::w(st), &tm_w, kt * (kPgBK / 2), n0, &bar_full[st]);
+        tma_load_2d(smem + L::sc(st), &tm_s, (kt >> 2) * 16, n0, &bar_full[st]);
+      }
     }
-    if (!mbar_wait_bounded(&bar_load[st], (kt / kPgStages) & 1, p.err)) s_bad = 1u;
-    __syncthreads();
-    if (s_bad) break;
-    // ---- decode this thread's weight row for k-step kt into the SW128 layout
-    if (tid < BN) {
-      const int row = tid;
-      const uint4* wp = reinterpret_cast<const uint4*>(smem + L::w(st) + row * (kPgBK / 2));
-      const uint4 w01 = wp[0], w23 = wp[1];
-      const uint32_t words[8] = {w01.x, w01.y, w01.z, w01.w, w23.x, w23.y, w23.z, w23.w};
-      const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(smem + L::sc(st) + row * 16 + (kt & 3) * 4);
+  } else if (warp == 1) {
+    // ---- MMA issuer: K steps go round-robin to the kPgAcc accumulators.
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = umma_idesc_bf16(kPgBM, BN);
+      for (int kt = 0; kt < nk; ++kt) {
+        const int st = kt % kPgStages, db = kt % kPgDec;
+        if (s_bad || !mbar_wait_bounded(&bar_full[st], (kt / kPgStages) & 1, p.err) ||
+            !mbar_wait_bounded(&bar_dfull[db], (kt / kPgDec) & 1, p.err)) {
+          s_bad = 1u;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t ad = umma_desc_sw128(smem_u32(smem + L::a(st)));
+        const uint64_t bd = umma_desc_sw128(smem_u32(smem + L::b(db)));
+        const uint32_t acc = tmem + static_cast<uint32_t>((kt % kPgAcc) * BN);
+#pragma unroll
+        for (int kk = 0; kk < kPgBK / 16; ++kk)  // +32 bytes of K per MMA inside the swizzle atom
+          umma_bf16(acc, ad + 2 * kk, bd + 2 * kk, kIdesc, (kt >= kPgAcc || kk > 0) ? 1u : 0u);
+        umma_commit(&bar_empty[st]);
+        umma_commit(&bar_dempty[db]);
+      }
+      umma_commit(&bar_acc);  // arrives once every MMA issued above is done
+    }
+    __syncwarp();
+  } else {
+    // ---- decoders: thread t of 256 decodes k [32*(t&1), +32) of row t>>1.
+    const int dt = tid - 64, row = dt >> 1, half = dt & 1;
+    for (int kt = 0; kt < nk; ++kt) {
+      const int st = kt % kPgStages, db = kt % kPgDec;
+      bool ok = !s_bad && mbar_wait_bounded(&bar_full[st], (kt / kPgStages) & 1, p.err);
+      if (ok && kt >= kPgDec) ok = mbar_wait_bounded(&bar_dempty[db], ((kt / kPgDec) - 1) & 1, p.err);
+      if (!__all_sync(0xffffffffu, ok)) {
+        s_bad = 1u;
+        break;
+      }
+      const uint4 wv = *reinterpret_cast<const uint4*>(smem + L::w(st) + row * (kPgBK / 2) + half * 16);
+      const uint32_t sc2 =
+          *reinterpret_cast<const uint16_t*>(smem + L::sc(st) + row * 16 + (kt & 3) * 4 + half * 2);
+      // The two block scales as BF16 (exact: UE4M3 has at most 4 significant bits).
+      uint32_t bh;
+      asm("{\n .reg .b16 lo;\n cvt.u16.u32 lo, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}" : "=r"(bh) : "r"(sc2));
+      const uint32_t beta2 = f16x2_to_bf16x2_exact(bh);
+      const uint32_t beta[2] = {__byte_perm(beta2, 0, 0x1010), __byte_perm(beta2, 0, 0x3232)};
+      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
       uint8_t* brow = smem + L::b(db) + row * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // chunk c = 8 k = word c
-        uint32_t beta;
-        asm("{\n .reg .b16 lo;\n cvt.u16.u32 lo, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}"
-            : "=r"(beta)
-            : "r"((sc4 >> (8 * (c >> 1))) & 0xffu));
-        beta = __byte_perm(beta, 0, 0x1010);
-        uint32_t h[4];
-        e2m1x8_to_f16x2x4(words[c], h);
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const __half2 q = __hmul2(*reinterpret_cast<const __half2*>(&h[j]), *reinterpret_cast<const __half2*>(&beta));
-          o[j] = f16x2_to_bf16x2_exact(*reinterpret_cast<const uint32_t*>(&q));
-        }
-        *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      for (int c = 0; c < 4; ++c) {  // 16-byte chunk half*4 + c = 8 k = word c
+        uint32_t q[4];
+        e2m1x8_to_bf16x2x4(words[c], q);
+        const uint32_t bt = beta[c >> 1];
+        // q * beta has at most 6 significant bits: the BF16 product is exact.
+        const int chunk = half * 4 + c;
+        *reinterpret_cast<uint4*>(brow + ((chunk ^ (row & 7)) << 4)) =
+            make_uint4(bf16x2_mul(q[0], bt), bf16x2_mul(q[1], bt), bf16x2_mul(q[2], bt), bf16x2_mul(q[3], bt));
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_dfull[db]);
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t ad = umma_desc_sw128(smem_u32(smem + L::a(st)));
-      const uint64_t bd = umma_desc_sw128(smem_u32(smem + L::b(db)));
-      const uint32_t acc = tmem + static_cast<uint32_t>((kt % kPgAcc) * BN);
-#pragma unroll
-      for (int kk = 0; kk < kPgBK / 16; ++kk)  // +32 bytes of K per MMA inside the swizzle atom
-        umma_bf16(acc, ad + 2 * kk, bd + 2 * kk, kIdesc, (kt >= kPgAcc || kk > 0) ? 1u : 0u);
-      umma_commit(&bar_mma[st]);
-    }
-  }
 
-  // ---- epilogue: accumulator lanes = tile rows
-  if (!s_bad && nk > 0 &&
-      !mbar_wait_bounded(&bar_mma[(nk - 1) % kPgStages], ((nk - 1) / kPgStages) & 1, p.err))
-    s_bad = 1u;
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (!s_bad) {
-    const float gamma = *p.gamma;
-    const int64_t row = m0 + warp * 32 + lane;
+    // ---- epilogue (warps 2-5): warp w reads tensor-memory lanes 32 * (w % 4).
+    if (warp < 6) {
+      const int quad = warp & 3;
+      const bool ok = !s_bad && nk > 0 && mbar_wait_bounded(&bar_acc, 0, p.err);
+      if (!ok) s_bad = 1u;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (__all_sync(0xffffffffu, ok)) {
+        const float gamma = *p.gamma;
+        const int64_t grow = m0 + quad * 32 + lane;
+        const uint32_t base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      // The accumulators that received K steps, added pairwise: ((a0 + a1) + (a2 + a3)) + ...
-      uint32_t v[32];
-      const uint32_t base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          // The accumulators that received K steps, added pairwise: ((a0 + a1) + (a2 + a3)).
+          uint32_t v[32];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float f[16];
-        tmem_sum_x16<kPgAcc>(base + c0 + 16 * half, BN, 0, nk, f);
+          for (int hh = 0; hh < 2; ++hh) {
+            float f[16];
+            tmem_sum_x16<kPgAcc>(base + c0 + 16 * hh, BN, 0, nk, f);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[16 * half + j] = __float_as_uint(f[j]);
-      }
-      if (row < p.m) {
-        uint16_t* dst = p.y + row * p.n + n0 + c0;
-        const int64_t cols = p.n - (n0 + c0);
-        if (cols >= 32 && (p.n % 8) == 0) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[8 * q + 2 * j]), gamma));
-              const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[8 * q + 2 * j + 1]), gamma));
-              pk[j] = lo | (hi << 16);
-            }
-            reinterpret_cast<uint4*>(dst)[q] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            for (int j = 0; j < 16; ++j) v[16 * hh + j] = __float_as_uint(f[j]);
           }
-        } else {
-          for (int j = 0; j < 32 && j < cols; ++j) dst[j] = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[j]), gamma));
+          if (grow < p.m) {
+            uint16_t* dst = p.y + grow * p.n + n0 + c0;
+            const int64_t cols = p.n - (n0 + c0);
+            if (cols >= 32 && (p.n % 8) == 0) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t lo = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[8 * q + 2 * j]), gamma));
+                  const uint32_t hi = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[8 * q + 2 * j + 1]), gamma));
+                  pk[j] = lo | (hi << 16);
+                }
+                reinterpret_cast<uint4*>(dst)[q] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
+            } else {
+              for (int j = 0; j < 32 && j < cols; ++j)
+                dst[j] = f32_to_bf16_bits(__fmul_rn(__uint_as_float(v[j]), gamma));
+            }
+          }
         }
       }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0)
+  if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN * kPgAcc) : "memory");
 }
 
