@@ -251,7 +251,9 @@ int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y,
 }
 
 // ---------------------------------------------------------------- tensor-core GEMM (prefill-sized M)
-constexpr int kPgBN = 128;  // x kPgAcc accumulators = 512 tensor-memory columns
+// 128 x 256 tiles: half the x traffic of 128 x 128 per FLOP and full-rate
+// N=256 MMAs; two accumulators of 256 columns fill the tensor memory.
+constexpr int kPgBN = 256;
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -304,7 +306,7 @@ int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t*
   if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM shared-memory opt-in");
   const dim3 grid(static_cast<unsigned>(ceil_div(n, kPgBN)), static_cast<unsigned>(ceil_div(m, kPgBM)));
   if (grid.y > 65535) return fail(NVFP4DA_ERR_UNSUPPORTED, "M too large for the tensor-core GEMM grid");
-  kern<<<grid, kPgThreads, smem, s>>>(tx, tw, ts, p);
+  kern<<<grid, PgCfg<kPgBN>::kThreads, smem, s>>>(tx, tw, ts, p);
   NVFP4DA_CHECK_LAUNCH("tensor-core GEMM launch");
   return NVFP4DA_OK;
 }

@@ -6,24 +6,26 @@
 // lies in [2^-10, 2688], so it is exact in BF16; BF16 x BF16 products are exact
 // in the FP32 accumulator, and gamma is applied once in the epilogue.
 //
-// One CTA computes a 128 x BN tile of y with tcgen05.mma (kind::f16, BF16
-// operands, FP32 accumulators in tensor memory), K in steps of 64, as a
-// warp-specialised pipeline on mbarriers:
-//  * warp 0 (one lane) streams, kPgStages steps ahead, the x tile [128 rows x
+// One CTA computes a 128 x BN tile (BN = 128 or 256) of y with tcgen05.mma
+// (kind::f16, BF16 operands, FP32 accumulators in tensor memory), K in steps
+// of 64, as a warp-specialised pipeline on mbarriers:
+//  * warp 0 (one lane) streams, kStages steps ahead, the x tile [128 rows x
 //    64 k] by TMA with 128-byte swizzle (the canonical K-major SW128 operand
-//    layout), the packed weight tile [BN x 32 bytes] and the scale tile
-//    [BN x 16 bytes];
-//  * warps 2-9 decode the weight tile (two threads per row, 32 k each) into
-//    one of kPgDec BF16 buffers in the SW128 K-major layout: E2M1 -> BF16 by
+//    layout) and the packed weight tile [BN x 32 bytes]; every fourth step
+//    also the scale tile [BN x 16 bytes] that covers four steps;
+//  * warps 2.. decode the weight tile (two threads per row, 32 k each) into
+//    one of kDec BF16 buffers in the SW128 K-major layout: E2M1 -> BF16 by
 //    byte permutes from two 8-entry tables (sign from the nibble's top bit),
 //    times the UE4M3 block scale in BF16, all exact;
 //  * warp 1 (one lane) issues the four K=16 MMAs of a step once its x tile and
-//    decoded buffer are ready, and commits them to the barriers that free the
+//    decoded buffer are ready, and commits them to one barrier that frees the
 //    load stage and the decoded buffer;
-//  * epilogue: warps 2-5 (one per 32-lane quarter of tensor memory) read the
-//    accumulators with tcgen05.ld, scale by gamma and store BF16.
-// Every wait is bounded; on expiry the kernel records kErrBarrierTimeout,
-// skips the remaining work, and still frees its tensor memory.
+//  * epilogue: the decode warps (warp w on the 32-lane quarter w % 4 of tensor
+//    memory, 64 columns each) read the accumulators with tcgen05.ld, scale by
+//    gamma and store BF16.
+// Every wait is bounded (one second); on expiry the kernel records
+// kErrBarrierTimeout, skips the remaining work, and still frees its tensor
+// memory.
 #pragma once
 
 #include <cuda.h>
@@ -34,12 +36,23 @@ namespace nvfp4da {
 
 constexpr int kPgBM = 128;
 constexpr int kPgBK = 64;
-constexpr int kPgThreads = 320;  // TMA warp, MMA warp, 8 decode warps
-constexpr int kPgDecodeWarps = 8;
-// K steps go round-robin to kPgAcc accumulators (TMEM column blocks) that the
-// epilogue adds in FP32: shorter accumulation chains keep the tensor cores'
-// internal rounding within one BF16 step of the correctly rounded sum.
-constexpr int kPgAcc = 4;
+// Per tile width BN: the decode warps (two threads per weight row), the
+// accumulators and the buffers.  K steps go round-robin to kAcc accumulators
+// (TMEM column blocks, 512 columns in all) that the epilogue adds in FP32:
+// shorter accumulation chains keep the tensor cores' internal rounding within
+// one BF16 step of the correctly rounded sum.
+template <int BN>
+struct PgCfg {
+  // Warp roles: warp 0 issues the TMA loads, warp 1 the MMAs, warps 2.. decode
+  // and then run the epilogue (a warp may only read tensor-memory lane
+  // quarter warp % 4; each takes 64 of the BN columns).
+  static constexpr int kDecodeWarps = BN / 16;
+  static constexpr int kThreads = 64 + 32 * kDecodeWarps;
+  static constexpr int kAcc = 512 / BN;
+  static constexpr int kStages = BN == 128 ? 8 : 6;  // x + packed-weight load stages in flight
+  static constexpr int kDec = 2;                     // decoded weight buffers
+  static constexpr int kScaleSlots = 3;              // scale tiles, one per 4 K steps
+};
 
 struct PgParams {
   int64_t m, n, k;
@@ -48,26 +61,27 @@ struct PgParams {
   unsigned* err;
 };
 
-// Load stages in flight (x tile, packed weights, scales) and decoded weight
-// buffers.
-constexpr int kPgStages = 6;
-constexpr int kPgDec = 3;
-
 // Shared-memory layout of one CTA (byte offsets from a 1024-aligned base).
 template <int BN>
 struct PgLayout {
+  using C = PgCfg<BN>;
   static constexpr uint32_t kA = kPgBM * kPgBK * 2;  // 16 KB per stage
-  static constexpr uint32_t kB = BN * kPgBK * 2;     // decoded weight tile per buffer
   static constexpr uint32_t kW = BN * kPgBK / 2;     // packed weight tile per stage
-  static constexpr uint32_t kS = BN * 16;            // scale bytes of 4 steps per stage
+  static constexpr uint32_t kB = BN * kPgBK * 2;     // decoded weight tile per buffer
+  static constexpr uint32_t kS = BN * 16;            // scale bytes of 4 K steps per slot
   __host__ __device__ static constexpr uint32_t a(int s) { return s * kA; }
-  __host__ __device__ static constexpr uint32_t b(int d) { return kPgStages * kA + d * kB; }
-  __host__ __device__ static constexpr uint32_t w(int s) { return kPgStages * kA + kPgDec * kB + s * kW; }
-  __host__ __device__ static constexpr uint32_t sc(int s) { return kPgStages * (kA + kW) + kPgDec * kB + s * kS; }
+  __host__ __device__ static constexpr uint32_t b(int d) { return C::kStages * kA + d * kB; }
+  __host__ __device__ static constexpr uint32_t w(int s) { return C::kStages * kA + C::kDec * kB + s * kW; }
+  __host__ __device__ static constexpr uint32_t sc(int g) {
+    return C::kStages * (kA + kW) + C::kDec * kB + g * kS;
+  }
   // + 1024 alignment slack.  One CTA per SM: it holds all 512 tensor-memory
   // columns.
-  __host__ __device__ static constexpr uint32_t total() { return kPgStages * (kA + kW + kS) + kPgDec * kB + 1024; }
-  static_assert(kPgStages * (kA + kW + kS) + kPgDec * kB + 1024 <= 227u * 1024, "shared memory per CTA");
+  __host__ __device__ static constexpr uint32_t total() {
+    return C::kStages * (kA + kW) + C::kDec * kB + C::kScaleSlots * kS + 1024;
+  }
+  static_assert(C::kStages * (kA + kW) + C::kDec * kB + C::kScaleSlots * kS + 1024 <= 227u * 1024,
+                "shared memory per CTA");
 };
 
 // ---------------------------------------------------------------- tcgen05 / TMA primitives
@@ -202,17 +216,50 @@ __device__ __forceinline__ uint32_t f16x2_to_bf16x2_exact(uint32_t h) {
 }
 
 // ---------------------------------------------------------------- the kernel
+// Bounded wait of the GEMM pipeline: try_wait until the phase with `parity`
+// completes; gives up (returns false) when another role already gave up
+// (`bad`) or after one second, recording kErrBarrierTimeout in `err`.
+__device__ __forceinline__ bool pg_wait(uint64_t* bar, uint32_t parity, volatile unsigned* bad, unsigned* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*bad) return false;
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > 1000000000ull) {
+        if (err) atomicOr(err, static_cast<unsigned>(kErrBarrierTimeout));
+        *bad = 1u;
+        return false;
+      }
+    }
+  }
+}
+
+// Pipeline (step kt = K columns [64 kt, 64 kt + 64)):
+//   full[s]   x tile + packed weights of step kt landed (s = kt % kStages);
+//   sfull[g]  scale tile of steps [4 g', 4 g' + 4) landed (g = g' % kScaleSlots);
+//   dfull[d]  every decode warp wrote decoded buffer d = kt % kDec;
+//   empty[s]  the MMAs of step kt are done (one tcgen05.commit per step): frees
+//             load stage s and decoded buffer kt % kDec, and, kStages steps on,
+//             the scale slot read four groups earlier;
+//   acc       every MMA is done (the epilogue may read tensor memory).
+// Every waiter is within one phase of the barrier it waits on: a later phase
+// needs work that itself waits for the waiter.
 template <int BN>
-__global__ void __launch_bounds__(kPgThreads, 1)
+__global__ void __launch_bounds__(PgCfg<BN>::kThreads, 1)
     w4a16_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                          const __grid_constant__ CUtensorMap tm_s, PgParams p) {
-  static_assert(BN == 128, "two decode threads per weight row: 8 warps cover 128 rows");
+  static_assert(BN == 128 || BN == 256, "N = 128 or 256 per MMA");
   using L = PgLayout<BN>;
+  using C = PgCfg<BN>;
+  constexpr int kSt = C::kStages, kDec = C::kDec, kAcc = C::kAcc, kSl = C::kScaleSlots;
+  static_assert(kSt > kDec && kSt <= 8, "stage reuse order");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // full: TMA bytes landed; empty: the step's MMAs are done with the stage;
-  // dfull: all decode warps wrote the buffer; dempty: its MMAs are done.
-  __shared__ uint64_t bar_full[kPgStages], bar_empty[kPgStages], bar_dfull[kPgDec], bar_dempty[kPgDec], bar_acc;
+  __shared__ uint64_t bar_full[kSt], bar_empty[kSt], bar_sfull[kSl], bar_dfull[kDec], bar_acc;
   __shared__ uint32_t tmem_base;
   __shared__ volatile unsigned s_bad;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -221,19 +268,17 @@ __global__ void __launch_bounds__(kPgThreads, 1)
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(BN * kPgAcc)
+                 "r"(BN * kAcc)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    for (int s = 0; s < kPgStages; ++s) {
+    for (int s = 0; s < kSt; ++s) {
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    for (int d = 0; d < kPgDec; ++d) {
-      mbar_init(&bar_dfull[d], kPgDecodeWarps);
-      mbar_init(&bar_dempty[d], 1);
-    }
+    for (int g = 0; g < kSl; ++g) mbar_init(&bar_sfull[g], 1);
+    for (int d = 0; d < kDec; ++d) mbar_init(&bar_dfull[d], C::kDecodeWarps);
     mbar_init(&bar_acc, 1);
     fence_mbar_init();
     s_bad = 0u;
@@ -244,60 +289,57 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   const uint32_t tmem = tmem_base;
 
   if (warp == 0) {
-    // ---- producer: stage kt % kPgStages is refilled once the MMAs of step
-    // kt - kPgStages are done.
+    // ---- producer.  Stage kt % kSt is refilled once the MMAs of step kt - kSt
+    // are done; scale slot (kt / 4) % kSl was last read by step kt - 9 at the
+    // latest, whose decode finished before MMA(kt - 9) was issued.
     if (lane == 0) {
-      for (int kt = 0; kt < nk && !s_bad; ++kt) {
-        const int st = kt % kPgStages;
-        if (kt >= kPgStages &&
-            !mbar_wait_bounded(&bar_empty[st], ((kt / kPgStages) - 1) & 1, p.err)) {
-          s_bad = 1u;
-          break;
+      for (int kt = 0; kt < nk; ++kt) {
+        const int st = kt % kSt;
+        if (kt >= kSt && !pg_wait(&bar_empty[st], ((kt / kSt) - 1) & 1, &s_bad, p.err)) break;
+        if ((kt & 3) == 0) {
+          const int g = kt >> 2;
+          mbar_arrive_expect_tx(&bar_sfull[g % kSl], L::kS);
+          tma_load_2d(smem + L::sc(g % kSl), &tm_s, g * 16, n0, &bar_sfull[g % kSl]);
         }
-        mbar_arrive_expect_tx(&bar_full[st], L::kA + L::kW + L::kS);
+        mbar_arrive_expect_tx(&bar_full[st], L::kA + L::kW);
         tma_load_2d(smem + L::a(st), &tm_x, kt * kPgBK, m0, &bar_full[st]);
         tma_load_2d(smem + L::w(st), &tm_w, kt * (kPgBK / 2), n0, &bar_full[st]);
-        tma_load_2d(smem + L::sc(st), &tm_s, (kt >> 2) * 16, n0, &bar_full[st]);
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer: K steps go round-robin to the kPgAcc accumulators.
+    // ---- MMA issuer: K steps go round-robin to the kAcc accumulators.
     if (lane == 0) {
       constexpr uint32_t kIdesc = umma_idesc_bf16(kPgBM, BN);
       for (int kt = 0; kt < nk; ++kt) {
-        const int st = kt % kPgStages, db = kt % kPgDec;
-        if (s_bad || !mbar_wait_bounded(&bar_full[st], (kt / kPgStages) & 1, p.err) ||
-            !mbar_wait_bounded(&bar_dfull[db], (kt / kPgDec) & 1, p.err)) {
-          s_bad = 1u;
+        const int st = kt % kSt, db = kt % kDec;
+        if (!pg_wait(&bar_full[st], (kt / kSt) & 1, &s_bad, p.err) ||
+            !pg_wait(&bar_dfull[db], (kt / kDec) & 1, &s_bad, p.err))
           break;
-        }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t ad = umma_desc_sw128(smem_u32(smem + L::a(st)));
         const uint64_t bd = umma_desc_sw128(smem_u32(smem + L::b(db)));
-        const uint32_t acc = tmem + static_cast<uint32_t>((kt % kPgAcc) * BN);
+        const uint32_t acc = tmem + static_cast<uint32_t>((kt % kAcc) * BN);
 #pragma unroll
         for (int kk = 0; kk < kPgBK / 16; ++kk)  // +32 bytes of K per MMA inside the swizzle atom
-          umma_bf16(acc, ad + 2 * kk, bd + 2 * kk, kIdesc, (kt >= kPgAcc || kk > 0) ? 1u : 0u);
+          umma_bf16(acc, ad + 2 * kk, bd + 2 * kk, kIdesc, (kt >= kAcc || kk > 0) ? 1u : 0u);
         umma_commit(&bar_empty[st]);
-        umma_commit(&bar_dempty[db]);
       }
       umma_commit(&bar_acc);  // arrives once every MMA issued above is done
     }
     __syncwarp();
   } else {
-    // ---- decoders: thread t of 256 decodes k [32*(t&1), +32) of row t>>1.
+    // ---- decoders: thread t of 2 * BN decodes k [32 (t & 1), +32) of row t >> 1.
     const int dt = tid - 64, row = dt >> 1, half = dt & 1;
     for (int kt = 0; kt < nk; ++kt) {
-      const int st = kt % kPgStages, db = kt % kPgDec;
-      bool ok = !s_bad && mbar_wait_bounded(&bar_full[st], (kt / kPgStages) & 1, p.err);
-      if (ok && kt >= kPgDec) ok = mbar_wait_bounded(&bar_dempty[db], ((kt / kPgDec) - 1) & 1, p.err);
-      if (!__all_sync(0xffffffffu, ok)) {
-        s_bad = 1u;
-        break;
-      }
+      const int st = kt % kSt, db = kt % kDec, g = kt >> 2;
+      bool ok = pg_wait(&bar_full[st], (kt / kSt) & 1, &s_bad, p.err) &&
+                pg_wait(&bar_sfull[g % kSl], (g / kSl) & 1, &s_bad, p.err);
+      // Decoded buffer db is free once the MMAs of step kt - kDec are done.
+      if (ok && kt >= kDec) ok = pg_wait(&bar_empty[(kt - kDec) % kSt], ((kt - kDec) / kSt) & 1, &s_bad, p.err);
+      if (!__all_sync(0xffffffffu, ok)) break;
       const uint4 wv = *reinterpret_cast<const uint4*>(smem + L::w(st) + row * (kPgBK / 2) + half * 16);
       const uint32_t sc2 =
-          *reinterpret_cast<const uint16_t*>(smem + L::sc(st) + row * 16 + (kt & 3) * 4 + half * 2);
+          *reinterpret_cast<const uint16_t*>(smem + L::sc(g % kSl) + row * 16 + (kt & 3) * 4 + half * 2);
       // The two block scales as BF16 (exact: UE4M3 has at most 4 significant bits).
       uint32_t bh;
       asm("{\n .reg .b16 lo;\n cvt.u16.u32 lo, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}" : "=r"(bh) : "r"(sc2));
@@ -306,7 +348,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
       const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
       uint8_t* brow = smem + L::b(db) + row * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 16-byte chunk half*4 + c = 8 k = word c
+      for (int c = 0; c < 4; ++c) {  // 16-byte chunk half * 4 + c = 8 k = word c
         uint32_t q[4];
         e2m1x8_to_bf16x2x4(words[c], q);
         const uint32_t bt = beta[c >> 1];
@@ -320,24 +362,24 @@ __global__ void __launch_bounds__(kPgThreads, 1)
       if (lane == 0) mbar_arrive(&bar_dfull[db]);
     }
 
-    // ---- epilogue (warps 2-5): warp w reads tensor-memory lanes 32 * (w % 4).
-    if (warp < 6) {
-      const int quad = warp & 3;
-      const bool ok = !s_bad && nk > 0 && mbar_wait_bounded(&bar_acc, 0, p.err);
-      if (!ok) s_bad = 1u;
+    // ---- epilogue (all decode warps): warp w reads tensor-memory lanes
+    // 32 * (w % 4) and 64 of the BN columns.
+    {
+      const int quad = warp & 3, cbase = ((warp - 2) >> 2) * 64;
+      const bool ok = nk > 0 && pg_wait(&bar_acc, 0, &s_bad, p.err) && !s_bad;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       if (__all_sync(0xffffffffu, ok)) {
         const float gamma = *p.gamma;
         const int64_t grow = m0 + quad * 32 + lane;
         const uint32_t base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          // The accumulators that received K steps, added pairwise: ((a0 + a1) + (a2 + a3)).
+        for (int c0 = cbase; c0 < cbase + 64; c0 += 32) {
+          // The accumulators that received K steps, added pairwise.
           uint32_t v[32];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             float f[16];
-            tmem_sum_x16<kPgAcc>(base + c0 + 16 * hh, BN, 0, nk, f);
+            tmem_sum_x16<kAcc>(base + c0 + 16 * hh, BN, 0, nk, f);
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[16 * hh + j] = __float_as_uint(f[j]);
           }
@@ -368,7 +410,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN * kPgAcc) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN * kAcc) : "memory");
 }
 
 }  // namespace nvfp4da
