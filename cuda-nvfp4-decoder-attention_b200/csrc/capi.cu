@@ -670,6 +670,10 @@ QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
 // one stream are ordered, so they never share a slot concurrently.
 constexpr int kStepSlots = 64;
 __device__ unsigned g_step_sync[kStepSlots][kStepSyncWords];
+// The step kernel's hand-off words (tagged, see decode_step.cuh), one region
+// per slot: only launches of that slot's stream ever write it, so a word can
+// carry the current tag only if this launch wrote it.
+__device__ unsigned long long g_step_tagged[kStepSlots][kStepTagWords];
 // Scratch words of the bounded-wait probe (nvfp4da_debug_wait_timeout).
 __device__ unsigned g_probe_words[4];
 
@@ -677,6 +681,7 @@ std::mutex g_slot_mutex;
 std::map<std::pair<int, uintptr_t>, int> g_slot_of;
 int g_slots_used[kMaxDevices] = {0};
 unsigned* g_slot_base[kMaxDevices] = {nullptr};
+unsigned long long* g_tag_base[kMaxDevices] = {nullptr};
 
 unsigned* slot_base_for_device(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return nullptr;
@@ -686,14 +691,21 @@ unsigned* slot_base_for_device(int dev) {
       cudaGetLastError();
       return nullptr;
     }
+    void* tags = nullptr;
+    if (cudaGetSymbolAddress(&tags, g_step_tagged) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
     g_slot_base[dev] = static_cast<unsigned*>(ptr);
+    g_tag_base[dev] = static_cast<unsigned long long*>(tags);
   }
   return g_slot_base[dev];
 }
 
 // The slot of `stream` on the current device (assigned on first use), or
-// nullptr when every slot is taken.
-unsigned* step_slot(cudaStream_t stream) {
+// nullptr when every slot is taken; *tagged (if given) = the slot's hand-off
+// region.
+unsigned* step_slot(cudaStream_t stream, unsigned long long** tagged = nullptr) {
   const int dev = current_device();
   std::lock_guard<std::mutex> lock(g_slot_mutex);
   unsigned* base = slot_base_for_device(dev);
@@ -708,6 +720,7 @@ unsigned* step_slot(cudaStream_t stream) {
     slot = g_slots_used[dev]++;
     g_slot_of[key] = slot;
   }
+  if (tagged) *tagged = g_tag_base[dev] + static_cast<size_t>(slot) * kStepTagWords;
   return base + static_cast<size_t>(slot) * kStepSyncWords;
 }
 
@@ -734,9 +747,9 @@ struct StepPlan {
   int epl, gh;
   int rq, n_qkv;
   int o_rows_big, o_n_big, o_rows_small, o_tile_rows;
-  int splits, split_len, grid, o_combine;
+  int splits, split_len, grid;
   uint32_t smem;
-  uint32_t off_qs, off_qw, off_kv, off_q, off_comb, off_os, off_ow, off_xs, off_x16, off_red;
+  uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
   size_t proj, ctx, part_o, part_ml, total;  // workspace offsets / bytes
 };
 
@@ -770,7 +783,6 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   if (group != 1 && group != 2 && group != 4 && group != 8) return false;
   const void* fn = step_kernel_ptr(epl, static_cast<int>(group));
   if (!fn) return false;
-  if (kSyncHeads + (hq + 2 * hkv) + nb * hkv > kStepSyncWords) return false;
   const std::pair<const nvfp4da_weight*, int> ws[4] = {{&a->q_weight, 0}, {&a->k_weight, 1}, {&a->v_weight, 2},
                                                        {&a->out_weight, 3}};
   for (auto& w : ws)
@@ -798,7 +810,14 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   const int64_t bh = nb * hkv;
   if (bh > grid) return false;
   const int64_t visible = (a->past_lengths ? a->max_past_length : a->past_length) + 1;
-  int64_t splits = std::max<int64_t>(1, std::min<int64_t>(grid / bh, ceil_div(visible, 64)));
+  // The hand-off words must fit the slot's region: projections and context
+  // (BF16 pairs) and every split's partials (FP32 singles).
+  const int64_t fixed_words = nb * nqkv / 2 + nb * k / 2 + 64;
+  const int64_t per_split_words = bh * group * (d + 2);
+  if (fixed_words + per_split_words > static_cast<int64_t>(kStepTagWords)) return false;
+  const int64_t max_splits = (static_cast<int64_t>(kStepTagWords) - fixed_words) / per_split_words;
+  int64_t splits = std::max<int64_t>(
+      1, std::min<int64_t>(std::min<int64_t>(grid / bh, max_splits), ceil_div(visible, 64)));
   const int64_t split_len = ceil_div(ceil_div(visible, splits), 8) * 8;
   splits = ceil_div(visible, split_len);
   s.epl = epl;
@@ -819,32 +838,15 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
     return static_cast<uint32_t>(o);
   };
   const uint64_t ks = k / 16, kb = k / 2;
-  // Overlay region: QKV rows, K/V tile (later the warps' o vectors and split
-  // weights) and q; after the attention unit, the split partials.
+  // Overlay region: QKV rows, K/V tile (later the warps' o vectors, then the
+  // split weights of the combine) and q.
   const uint64_t tile = 2ull * split_len * d * 2, smo = 1ull * kStepWarps * group * d * 4,
-                 comb_w = 1ull * group * splits * 4;
+                 comb_w = 2ull * group * splits * 4;
   s.off_qs = take(rq * ks);
   s.off_qw = take(rq * kb);
   s.off_kv = take(std::max(tile, std::max(smo, comb_w)));
   s.off_q = take(group * d * 4);
-  const uint64_t front = off;
   const uint64_t items = nb * hq;
-  const uint64_t comb = items * splits * d * 4 + items * splits * 16;
-  // The O CTAs combine the partials themselves when they fit beside the rest.
-  s.o_combine = 0;
-  off = std::max(front, comb);
-  s.off_comb = 0;
-  const uint64_t rest = (rows_big * ks + 127) / 128 * 128 + (rows_big * kb + 127) / 128 * 128 +
-                        2 * ((nb * k * 2 + 127) / 128 * 128) + kMmaWarps * 128 * 4;
-  // Measured on B200: all 148 CTAs bulk-reading the same partials is slower
-  // than the last-arriver combine, so the combine-in-O variant stays off by
-  // default (kept for configurations with few, small partials).
-  constexpr bool kPreferOCombine = false;
-  if (kPreferOCombine && off + rest + static_smem(fn) <= kMaxDynSmem) {
-    s.o_combine = 1;
-  } else {
-    off = front;
-  }
   s.off_os = take(rows_big * ks);
   s.off_ow = take(rows_big * kb);
   s.off_xs = take(nb * k * 2);
@@ -855,22 +857,26 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   // land in the buffers that follow (in bounds, their outputs discarded).
   if (s.off_ow + static_cast<uint64_t>(s.o_tile_rows) * kb > off) return false;
   s.smem = static_cast<uint32_t>(off);
+  // Word offsets in the slot's hand-off region: BF16 pairs for the
+  // projections and the context, single FP32 values for the partials.
   size_t w = 0;
   s.proj = w;
-  w += align_up(static_cast<size_t>(nb * nqkv) * 2, 256);
+  w += static_cast<size_t>(nb * nqkv / 2);
   s.ctx = w;
-  w += align_up(static_cast<size_t>(nb * k) * 2, 256);
+  w += static_cast<size_t>(nb * k / 2);
   s.part_o = w;
-  w += align_up(static_cast<size_t>(items) * splits * d * 4, 256);
+  w += static_cast<size_t>(items) * splits * d;
   s.part_ml = w;
-  w += align_up(static_cast<size_t>(items) * splits * 16, 256);
-  s.total = w;
+  w += static_cast<size_t>(items) * splits * 2;
+  if (w > kStepTagWords) return false;
+  s.total = 256;  // the step keeps nothing in the caller's workspace
   return true;
 }
 
 int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaStream_t stream) {
-  unsigned* slot = step_slot(stream);
-  if (!slot) return fail(NVFP4DA_ERR_UNSUPPORTED, "no free synchronisation slot for another stream");
+  unsigned long long* tagged = nullptr;
+  unsigned* slot = step_slot(stream, &tagged);
+  if (!slot || !tagged) return fail(NVFP4DA_ERR_UNSUPPORTED, "no free synchronisation slot for another stream");
   StepParams p{};
   p.x = a->x;
   p.g_in = a->input_norm_weight;
@@ -904,24 +910,22 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   p.o_tile_rows = pl.o_tile_rows;
   p.splits = pl.splits;
   p.split_len = pl.split_len;
-  p.o_combine = pl.o_combine;
-  char* base = static_cast<char*>(ws);
-  p.proj = reinterpret_cast<uint16_t*>(base + pl.proj);
-  p.ctx = reinterpret_cast<uint16_t*>(base + pl.ctx);
-  p.part_o = reinterpret_cast<float*>(base + pl.part_o);
-  p.part_ml = reinterpret_cast<float*>(base + pl.part_ml);
+  (void)ws;
+  p.proj = tagged + pl.proj;
+  p.ctx = tagged + pl.ctx;
+  p.part_o = tagged + pl.part_o;
+  p.part_ml = tagged + pl.part_ml;
+  p.tag_words = kStepTagWords;
   p.sync = slot;
   p.timeout_ns = 500ull * 1000 * 1000;
   p.sched = 1;
 #ifdef NVFP4DA_PHASES
   if (const char* v = std::getenv("NVFP4DA_STEP_SCHED")) p.sched = std::atoi(v);
-  if (const char* v = std::getenv("NVFP4DA_STEP_OCOMB")) p.o_combine = p.o_combine && std::atoi(v);
 #endif
   p.off_qs = pl.off_qs;
   p.off_qw = pl.off_qw;
   p.off_kv = pl.off_kv;
   p.off_q = pl.off_q;
-  p.off_comb = pl.off_comb;
   p.off_os = pl.off_os;
   p.off_ow = pl.off_ow;
   p.off_xs = pl.off_xs;

@@ -19,25 +19,29 @@
 //  * QKV block c: concatenated rows [c*RQ, c*RQ + RQ) of [Wq; Wk; Wv]
 //    (RQ divides D, so a block lies in one head).  Each CTA recomputes the
 //    input RMSNorm of the activation rows itself (tiny, L2-resident), runs the
-//    tensor-core GEMV from shared memory and writes the raw BF16 projections
-//    to the workspace, then bumps its head's counter.
+//    tensor-core GEMV from shared memory and publishes the raw BF16
+//    projections.
 //  * Attention unit (b, kv head, split j): positions [j*L, j*L + L) of
-//    sequence b.  Waits for the counters of its GH query heads and its K and V
-//    head, applies the per-head RMSNorm + RoPE to those rows itself, appends
-//    the new K/V row to the cache (the split holding position P_b), runs the
-//    online-softmax loop over its K/V tile, and leaves (m, l, o) partials.
-//  * O block c: 8-row multiples of Wo (the rows spread over all CTAs).  When
-//    every split's partials fit in shared memory (o_combine) each O CTA
-//    bulk-copies all of them once every unit has signalled and does the
-//    log-sum-exp combine itself -- no extra hand-off; otherwise the last split
-//    of each (b, kv head) to arrive combines them into a BF16 context buffer
-//    that the O CTAs read.
+//    sequence b.  Takes the projections of its GH query heads and its K and V
+//    head as they are published, applies the per-head RMSNorm + RoPE to those
+//    rows itself, appends the new K/V row to the cache (the split holding
+//    position P_b), runs the online-softmax loop over its K/V tile and
+//    publishes (m, l, o) partials.  Then the splits of (b, kv head) combine
+//    together: split j takes every split's partials for its share of the
+//    GH x D context and publishes that share as BF16.
+//  * O block c: 8-row multiples of Wo (the rows spread over all CTAs): takes
+//    the context as it is published and runs the O GEMV.
 //
-// Synchronisation state lives in a slot of library-owned device memory (one
-// slot per stream), zero between launches: the last CTA to leave clears it.
-// Every wait is bounded by a time limit; on expiry the kernel records
-// kErrBarrierTimeout in the slot and carries on (results are then garbage, the
-// GPU stays usable).
+// Hand-offs between CTAs carry their own validity: every published value is
+// a 64-bit word (32 bits of data, 32 bits of tag) stored and polled with
+// relaxed gpu-scope accesses, which are single-copy atomic.  The words live
+// in the stream's slot of library-owned device memory, written only by this
+// stream's step launches; the tag is the launch's epoch (kept in the slot,
+// advanced by the last CTA to leave), so no value of an earlier launch
+// passes for this launch's.  One round trip through L2 per hand-off: no
+// separate counter to release and acquire.  Every wait is bounded by a time
+// limit; on expiry the kernel records kErrBarrierTimeout in the slot and
+// carries on (results are then garbage, the GPU stays usable).
 #pragma once
 
 #include "attention.cuh"
@@ -52,7 +56,8 @@ constexpr int kStepWarps = kMmaWarps;
 constexpr int kStepMaxRows = 128;    // RQ / RO rows per CTA (tile-padded)
 constexpr int kStepSyncWords = 2048;  // one slot
 // Slot layout (32-bit words).
-constexpr int kSyncExit = 0, kSyncCtxDone = 1, kSyncErr = 2, kSyncHeads = 16;
+constexpr int kSyncExit = 0, kSyncEpoch = 1, kSyncErr = 2;
+constexpr size_t kStepTagWords = 65536;  // hand-off words per slot (512 KB)
 
 struct StepParams {
   const uint16_t* x;     // [B, H]
@@ -73,12 +78,12 @@ struct StepParams {
   int rq, n_qkv_blocks;                        // QKV rows per block (divides D)
   int o_rows_big, o_n_big, o_rows_small, o_tile_rows;  // O rows per CTA: big for CTAs < o_n_big
   int splits, split_len;
-  int o_combine;  // 1: O CTAs combine the split partials themselves
-  // workspace
-  uint16_t* proj;    // [B, (Hq + 2 Hkv) D] raw projections
-  uint16_t* ctx;     // [B, H]            (o_combine == 0)
-  float* part_o;     // [B * Hq, splits, D]
-  float* part_ml;    // [B * Hq, splits, 4]  (m, l, -, -)
+  // the slot's hand-off region: tagged words (low 32 bits data, high 32 bits tag)
+  unsigned long long* proj;     // [B, (Hq + 2 Hkv) D / 2] raw projections, BF16 pairs
+  unsigned long long* ctx;      // [B, H / 2]              context, BF16 pairs
+  unsigned long long* part_o;   // [B * Hq, splits, D]     FP32
+  unsigned long long* part_ml;  // [B * Hq, splits, 2]     FP32 (m, l)
+  size_t tag_words;             // the region's size, cleared when the epoch wraps
   unsigned* sync;    // slot
   unsigned long long timeout_ns;
   // When the K/V tile and the O rows are requested: 0 at launch, 1 once the
@@ -86,7 +91,7 @@ struct StepParams {
   // attention unit.
   int sched;
   // dynamic shared-memory layout (byte offsets); qs/qw/kv/q and comb overlay
-  uint32_t off_qs, off_qw, off_kv, off_q, off_comb, off_os, off_ow, off_xs, off_x16, off_red;
+  uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
   // cos/sin of RoPE at position past_length (rope_host_ok), else computed on the device
   int rope_host_ok;
   float2 rope_host[kMaxHeadDim / 2];
@@ -142,18 +147,59 @@ __device__ __forceinline__ void cta_wait(const unsigned* ctr, const int* idx, in
   __syncthreads();
 }
 
+// Tagged words: 32 bits of data (low) and the launch's tag (high).
+__device__ __forceinline__ void st_tagged(unsigned long long* p, uint32_t v, uint32_t tag) {
+  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | v;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+// Poll N tagged words of this thread at once until all carry `tag` or the
+// deadline passes (then the timeout is recorded in *err and the last values
+// read are returned).  Each round costs one L2 round trip for all N.
+template <int N>
+__device__ __forceinline__ void poll_tagged(const unsigned long long* const (&src)[N], uint32_t (&out)[N],
+                                            uint32_t tag, unsigned long long deadline, unsigned* err) {
+  uint32_t have = 0;
+  for (;;) {
+    unsigned long long w[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (!(have >> i & 1u)) w[i] = ld_tagged(src[i]);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (!(have >> i & 1u) && static_cast<uint32_t>(w[i] >> 32) == tag) {
+        out[i] = static_cast<uint32_t>(w[i]);
+        have |= 1u << i;
+      }
+    if (have == (1u << N) - 1u) return;
+    if (global_ns() > deadline) {
+      atomicOr(err, static_cast<unsigned>(kErrBarrierTimeout));
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if (!(have >> i & 1u)) out[i] = static_cast<uint32_t>(w[i]);
+      return;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- the kernel
 template <int EPL, int GH>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t bar_qkv, bar_kv, bar_o, bar_c;
+  __shared__ uint64_t bar_qkv, bar_kv, bar_o;
   __shared__ float redf[2 * kStepWarps];
   __shared__ double redd[2 * kStepWarps];
   __shared__ float escale[kMmaMaxM];
   __shared__ float red_small[kMmaMaxM * kStepWarps];
   __shared__ float outv[kStepMaxRows * 8];
   __shared__ float sm_m[kStepWarps][GH], sm_l[kStepWarps][GH], wf[kStepWarps][GH], cta_m[GH], cta_l[GH];
-  __shared__ unsigned s_flag;
+  __shared__ unsigned s_flag, s_tag;
   [[maybe_unused]] constexpr unsigned kPhaseBase = 3072;
   constexpr int PPL = EPL / 2;  // RoPE pairs per lane (D = 32 * EPL)
   NVFP4DA_PHASE(0);
@@ -176,8 +222,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   const int ns = p.splits;
   unsigned* sync = p.sync;
   unsigned* err = sync + kSyncErr;
-  unsigned* head_done = sync + kSyncHeads;        // [Hq + 2 Hkv]
-  unsigned* arrive = head_done + (hq + 2 * hkv);  // [B * Hkv]
 
   uint8_t* qs_smem = smem + p.off_qs;
   uint8_t* qw_smem = smem + p.off_qw;
@@ -238,13 +282,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   }
 
   if (threadIdx.x == 0) {
+    s_tag = *reinterpret_cast<volatile unsigned*>(sync + kSyncEpoch) + 1u;  // 1 .. 2^32 - 1
     mbar_init(&bar_qkv, 1);
     mbar_init(&bar_kv, 1);
     mbar_init(&bar_o, 1);
-    mbar_init(&bar_c, 1);
     fence_mbar_init();
   }
   __syncthreads();
+  const uint32_t tag = s_tag;
+  const unsigned long long deadline = global_ns() + p.timeout_ns;
 
   // ---- input slices of this CTA (none is written by the step): the QKV
   // rows now, the K/V tile and the O rows later (p.sched), so that they do
@@ -306,25 +352,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       mma_gemv_pass_smem<false, 4>(qw_smem, qs_smem, x_stage, k, p.rq, p.rq, mrows, mred, outv);
     NVFP4DA_PHASE(13);
     const float gamma = *p.gamma[mat];
-    for (int i = threadIdx.x; i < p.rq * mrows; i += kStepThreads) {
-      const int n = i / p.rq, r = i % p.rq;
-      const float v = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
-      p.proj[n * nqkv + qrow0 + r] = f32_to_bf16_bits(__fmul_rn(v, gamma));
+    const int rq2 = p.rq / 2;  // BF16 pairs (RQ and the row offsets are even)
+    for (int i = threadIdx.x; i < rq2 * mrows; i += kStepThreads) {
+      const int n = i / rq2, r = 2 * (i % rq2);
+      const float v0 = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
+      const float v1 = f16 ? outv[(r + 1) * 8 + n] * escale[n] : outv[(r + 1) * 8 + n];
+      const uint32_t pair = f32_to_bf16_bits(__fmul_rn(v0, gamma)) |
+                            (static_cast<uint32_t>(f32_to_bf16_bits(__fmul_rn(v1, gamma))) << 16);
+      st_tagged(p.proj + (n * nqkv + qrow0 + r) / 2, pair, tag);
     }
-    cta_signal(&head_done[qrow0 / d]);
     NVFP4DA_PHASE(4);
   }
 
   // ---- attention unit
   if (has_attn) {
-    {
-      __shared__ int widx[GH + 2];
-      if (threadIdx.x < GH) widx[threadIdx.x] = static_cast<int>(kvh * GH + threadIdx.x);
-      if (threadIdx.x == GH) widx[GH] = static_cast<int>(hq + kvh);
-      if (threadIdx.x == GH + 1) widx[GH + 1] = static_cast<int>(hq + hkv + kvh);
-      __syncthreads();
-      cta_wait(head_done, widx, GH + 2, static_cast<unsigned>(d / p.rq), err, p.timeout_ns);
-    }
     NVFP4DA_PHASE(5);
     // Per-head RMSNorm + RoPE of this unit's query heads (and, for the split
     // holding position P_b, of the new key; the new value is the raw
@@ -335,10 +376,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       const bool is_q = item < GH;
       if (!is_q && !owns_new) continue;
       const int64_t col = is_q ? (kvh * GH + item) * d : (item == GH ? (hq + kvh) * d : (hq + hkv + kvh) * d);
-      const uint32_t* y2 = reinterpret_cast<const uint32_t*>(p.proj + b * nqkv + col);
-      uint32_t pr2[PPL];
+      const unsigned long long* y2 = p.proj + (b * nqkv + col) / 2;
+      const unsigned long long* src[PPL];
 #pragma unroll
-      for (int j = 0; j < PPL; ++j) pr2[j] = __ldcg(y2 + lane + 32 * j);
+      for (int j = 0; j < PPL; ++j) src[j] = y2 + lane + 32 * j;
+      uint32_t pr2[PPL];
+      poll_tagged<PPL>(src, pr2, tag, deadline, err);
       if (item == GH + 1) {
         uint32_t* dst = reinterpret_cast<uint32_t*>(p.v_cache + ((b * hkv + kvh) * p.capacity + pb) * d);
         uint32_t* tile = reinterpret_cast<uint32_t*>(kv_v + nslot * d);
@@ -500,9 +543,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       }
       cta_m[g] = mx;
       cta_l[g] = l;
-      float* ml = p.part_ml + ((b * hq + kvh * GH + g) * ns + split) * 4;
-      ml[0] = mx;
-      ml[1] = l;
+      unsigned long long* ml = p.part_ml + ((b * hq + kvh * GH + g) * ns + split) * 2;
+      st_tagged(ml, __float_as_uint(mx), tag);
+      st_tagged(ml + 1, __float_as_uint(l), tag);
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < GH * d; idx += kStepThreads) {
@@ -511,48 +554,68 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       float o = 0.0f;
 #pragma unroll
       for (int w = 0; w < kStepWarps; ++w) o = fmaf(sm_o[(w * GH + g) * 32 * EPL + e], wf[w][g], o);
-      p.part_o[((b * hq + kvh * GH + g) * ns + split) * d + e] = o;
+      st_tagged(p.part_o + ((b * hq + kvh * GH + g) * ns + split) * d + e, __float_as_uint(o), tag);
     }
-    if (p.o_combine) {
-      cta_signal(&sync[kSyncCtxDone]);  // counts units
-    } else {
-      // The last split of (b, kv head) to arrive combines all of them.
+    // The splits of (b, kv head) combine together: split j takes pairs
+    // [j * share, j * share + share) of the GH x D context, every split's
+    // partials for them in split order (the log-sum-exp combine of reference
+    // decoder_attention.py's softmax).
+    {
+      float* sw = sm_o;  // [GH][ns] weights exp(m_s - M); the o vectors are consumed
       __syncthreads();
-      if (threadIdx.x == 0) {
-        const unsigned prev = atom_add_acq_rel(&arrive[bh], 1u);
-        s_flag = prev == static_cast<unsigned>(ns - 1) ? 1u : 0u;
+      for (int it = threadIdx.x; it < GH * ns; it += kStepThreads) {
+        const int g = it / ns, sp = it % ns;
+        const unsigned long long* mlp = p.part_ml + ((b * hq + kvh * GH + g) * ns + sp) * 2;
+        const unsigned long long* src[2] = {mlp, mlp + 1};
+        uint32_t v[2];
+        poll_tagged<2>(src, v, tag, deadline, err);
+        sw[it] = __uint_as_float(v[0]);               // m_s
+        sw[GH * ns + it] = __uint_as_float(v[1]);     // l_s
       }
       __syncthreads();
-      if (s_flag) {
-        NVFP4DA_PHASE(8);
-        float* sw = sm_o;  // free again: weights exp(m_s - M)
-        for (int g = warp; g < GH; g += kStepWarps) {
-          const float* ml = p.part_ml + (b * hq + kvh * GH + g) * ns * 4;
-          float mx = -INFINITY;
-          for (int sp = lane; sp < ns; sp += 32) mx = fmaxf(mx, __ldcg(ml + sp * 4));
-          mx = warp_max_f32(mx);
-          float l = 0.0f;
-          for (int sp = lane; sp < ns; sp += 32) {
-            const float ms = __ldcg(ml + sp * 4);
-            const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
-            sw[g * ns + sp] = f;
-            l = fmaf(__ldcg(ml + sp * 4 + 1), f, l);
+      if (threadIdx.x < GH) {
+        const int g = threadIdx.x;
+        float mx = -INFINITY;
+        for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, sw[g * ns + sp]);
+        float l = 0.0f;
+        for (int sp = 0; sp < ns; ++sp) {
+          const float ms = sw[g * ns + sp];
+          const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
+          sw[g * ns + sp] = f;
+          l = fmaf(sw[GH * ns + g * ns + sp], f, l);
+        }
+        cta_l[g] = l;
+      }
+      __syncthreads();
+      const int pairs = GH * static_cast<int>(d) / 2;
+      const int share = (pairs + ns - 1) / ns;
+      const int lo = split * share, hi = lo + share < pairs ? lo + share : pairs;
+      for (int pi = lo + threadIdx.x; pi < hi; pi += kStepThreads) {
+        const int g = (2 * pi) / static_cast<int>(d);
+        const int64_t e = (2 * pi) % d;
+        const int64_t row = b * hq + kvh * GH + g;
+        float o0 = 0.0f, o1 = 0.0f;
+        for (int sp0 = 0; sp0 < ns; sp0 += 4) {
+          const unsigned long long* src[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int sp = sp0 + j < ns ? sp0 + j : ns - 1;
+            src[2 * j] = p.part_o + (row * ns + sp) * d + e;
+            src[2 * j + 1] = src[2 * j] + 1;
           }
-          l = warp_sum_f32(l);
-          if (lane == 0) cta_l[g] = l;
+          uint32_t v[8];
+          poll_tagged<8>(src, v, tag, deadline, err);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (sp0 + j < ns) {
+              const float f = sw[g * ns + sp0 + j];
+              o0 = fmaf(__uint_as_float(v[2 * j]), f, o0);
+              o1 = fmaf(__uint_as_float(v[2 * j + 1]), f, o1);
+            }
         }
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < GH * d; idx += kStepThreads) {
-          const int g = static_cast<int>(idx / d);
-          const int64_t e = idx % d;
-          const int64_t row = b * hq + kvh * GH + g;
-          const float* src = p.part_o + row * ns * d + e;
-          float o = 0.0f;
-#pragma unroll 8
-          for (int sp = 0; sp < ns; ++sp) o = fmaf(__ldcg(src + sp * d), sw[g * ns + sp], o);
-          p.ctx[row * d + e] = f32_to_bf16_bits(__fdiv_rn(o, cta_l[g]));
-        }
-        cta_signal(&sync[kSyncCtxDone]);  // counts (b, kv head) groups
+        const uint32_t pair = f32_to_bf16_bits(__fdiv_rn(o0, cta_l[g])) |
+                              (static_cast<uint32_t>(f32_to_bf16_bits(__fdiv_rn(o1, cta_l[g]))) << 16);
+        st_tagged(p.ctx + (b * k + (kvh * GH + g) * d + e) / 2, pair, tag);
       }
     }
     if (threadIdx.x == 0 && (p.sched & 7) == 2 && has_qkv) issue_o();
@@ -561,55 +624,27 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   // ---- O projection
   if (has_o) {
+    // The context, as the splits publish it, into the BF16 operand rows.
     {
-      const int idx0 = kSyncCtxDone;
-      const unsigned target = p.o_combine ? static_cast<unsigned>(n_units) : static_cast<unsigned>(nb * hkv);
-      cta_wait(sync, &idx0, 1, target, err, p.timeout_ns);
-    }
-    NVFP4DA_PHASE(10);
-    bool f16;
-    if (p.o_combine) {
-      // Every split's partials in one bulk copy (the QKV/KV region is dead),
-      // then the log-sum-exp combine of reference decoder_attention.py's
-      // softmax, split by split in order, per (row, head) item.
-      float* co = reinterpret_cast<float*>(smem + p.off_comb);
-      const int64_t items = nb * hq;
-      float* cml = co + items * ns * d;
-      if (threadIdx.x == 0) {
-        const uint32_t ob = static_cast<uint32_t>(items * ns * d * 4), mb = static_cast<uint32_t>(items * ns * 16);
-        asm volatile("fence.proxy.async.global;" ::: "memory");  // acquired generic writes -> bulk reads
-        mbar_arrive_expect_tx(&bar_c, ob + mb);
-        bulk_g2s(co, p.part_o, ob, &bar_c);
-        bulk_g2s(cml, p.part_ml, mb, &bar_c);
-      }
-      mbar_wait_bounded(&bar_c, 0, err);
-      for (int64_t it = warp; it < items; it += kStepWarps) {
-        const float* ml = cml + it * ns * 4;
-        float mx = -INFINITY;
-        for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, ml[sp * 4]);
-        float l = 0.0f, o[EPL];
+      const int pairs = static_cast<int>(nb * k / 2);
+      uint32_t* xs2 = reinterpret_cast<uint32_t*>(x_stage);
+      for (int i0 = threadIdx.x; i0 < pairs; i0 += 4 * kStepThreads) {
+        const unsigned long long* src[4];
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
-        const float* ob = co + it * ns * d + lane * EPL;
-        for (int sp = 0; sp < ns; ++sp) {
-          const float ms = ml[sp * 4];
-          const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
-          l = fmaf(ml[sp * 4 + 1], f, l);
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) o[e] = fmaf(ob[sp * d + e], f, o[e]);
+        for (int j = 0; j < 4; ++j) {
+          const int i = i0 + j * kStepThreads;
+          src[j] = p.ctx + (i < pairs ? i : i0);
         }
-        const int64_t m = it / hq, h = it % hq;
-        uint16_t* dst = x_stage + m * k + h * d + lane * EPL;
+        uint32_t v[4];
+        poll_tagged<4>(src, v, tag, deadline, err);
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) dst[e] = f32_to_bf16_bits(__fdiv_rn(o[e], l));
+        for (int j = 0; j < 4; ++j)
+          if (i0 + j * kStepThreads < pairs) xs2[i0 + j * kStepThreads] = v[j];
       }
       __syncthreads();
-      NVFP4DA_PHASE(14);
-      f16 = mma_prepare_f16(x_stage, x16, k, mrows, escale, red_small);
-    } else {
-      const uint4 none[NCH] = {};
-      f16 = prep_rows_regs<NCH, false, true>(p.ctx, k, mrows, none, 0.0f, x_stage, x16, escale, redf, redd, nullptr);
     }
+    NVFP4DA_PHASE(10);
+    const bool f16 = mma_prepare_f16(x_stage, x16, k, mrows, escale, red_small);
     mbar_wait_bounded(&bar_o, 0, err);
     NVFP4DA_PHASE(11);
     if (f16)
@@ -626,7 +661,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     NVFP4DA_PHASE(12);
   }
 
-  // ---- leave; the last CTA out clears the slot's counters for the next launch
+  // ---- leave; the last CTA out resets the exit counter and advances the epoch
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned prev = atom_add_acq_rel(&sync[kSyncExit], 1u);
@@ -634,11 +669,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   }
   __syncthreads();
   if (s_flag) {
-    const int64_t words = (hq + 2 * hkv) + nb * hkv;
-    for (int64_t i = threadIdx.x; i < words; i += kStepThreads) head_done[i] = 0u;
+    // Tags run 1, 2, ..., 2^32 - 1 (the region starts zeroed, and 0 is never
+    // a tag); before they wrap, the region is cleared so that no word of an
+    // old launch can carry a reused tag.
+    if (tag == 0xFFFFFFFFu) {
+      unsigned long long* region = p.proj;  // the region's first word
+      for (size_t i = threadIdx.x; i < p.tag_words; i += kStepThreads) region[i] = 0ull;
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
-      sync[kSyncCtxDone] = 0u;
       sync[kSyncExit] = 0u;
+      sync[kSyncEpoch] = tag == 0xFFFFFFFFu ? 0u : tag;  // the next launch tags with epoch + 1
     }
   }
 }
