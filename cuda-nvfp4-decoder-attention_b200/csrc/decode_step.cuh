@@ -165,6 +165,8 @@ __device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long
 template <int N>
 __device__ __forceinline__ void poll_tagged(const unsigned long long* const (&src)[N], uint32_t (&out)[N],
                                             uint32_t tag, unsigned long long deadline, unsigned* err) {
+  static_assert(N >= 1 && N <= 32, "at most 32 words per poll");
+  constexpr uint32_t kAll = N == 32 ? 0xFFFFFFFFu : (1u << (N & 31)) - 1u;
   uint32_t have = 0;
   for (;;) {
     unsigned long long w[N];
@@ -177,7 +179,7 @@ __device__ __forceinline__ void poll_tagged(const unsigned long long* const (&sr
         out[i] = static_cast<uint32_t>(w[i]);
         have |= 1u << i;
       }
-    if (have == (1u << N) - 1u) return;
+    if (have == kAll) return;
     if (global_ns() > deadline) {
       atomicOr(err, static_cast<unsigned>(kErrBarrierTimeout));
 #pragma unroll
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   __shared__ float red_small[kMmaMaxM * kStepWarps];
   __shared__ float outv[kStepMaxRows * 8];
   __shared__ float sm_m[kStepWarps][GH], sm_l[kStepWarps][GH], wf[kStepWarps][GH], cta_m[GH], cta_l[GH];
-  __shared__ unsigned s_flag, s_tag;
+  __shared__ unsigned s_flag;
   [[maybe_unused]] constexpr unsigned kPhaseBase = 3072;
   constexpr int PPL = EPL / 2;  // RoPE pairs per lane (D = 32 * EPL)
   NVFP4DA_PHASE(0);
@@ -269,6 +271,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   const uint16_t* kbase = p.k_cache + (b * hkv + kvh) * p.capacity * d;
   const uint16_t* vbase = p.v_cache + (b * hkv + kvh) * p.capacity * d;
 
+  // This launch's tag (1 .. 2^32 - 1): every thread loads the epoch word now
+  // and first uses it microseconds later, so the load's latency is hidden.
+  uint32_t epoch;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(epoch) : "l"(sync + kSyncEpoch) : "memory");
+  const uint32_t tag = epoch + 1u;
+
   // ---- the activation rows and the input-norm gain first: they head the
   // critical path, so their requests go out before any bulk traffic.
   constexpr int NCH = 2;
@@ -282,14 +290,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   }
 
   if (threadIdx.x == 0) {
-    s_tag = *reinterpret_cast<volatile unsigned*>(sync + kSyncEpoch) + 1u;  // 1 .. 2^32 - 1
     mbar_init(&bar_qkv, 1);
     mbar_init(&bar_kv, 1);
     mbar_init(&bar_o, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  const uint32_t tag = s_tag;
   const unsigned long long deadline = global_ns() + p.timeout_ns;
 
   // ---- input slices of this CTA (none is written by the step): the QKV
@@ -560,7 +566,46 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     // [j * share, j * share + share) of the GH x D context, every split's
     // partials for them in split order (the log-sum-exp combine of reference
     // decoder_attention.py's softmax).
-    {
+    const int pairs = GH * static_cast<int>(d) / 2;
+    const int share = (pairs + ns - 1) / ns;
+    const int lo = split * share, hi = lo + share < pairs ? lo + share : pairs;
+    if (ns <= 8) {
+      // Every split's (m, l) and o for this thread's pair in one poll: one
+      // round trip once the slowest split has published.
+      for (int pi = lo + threadIdx.x; pi < hi; pi += kStepThreads) {
+        const int g = (2 * pi) / static_cast<int>(d);
+        const int64_t e = (2 * pi) % d;
+        const int64_t row = b * hq + kvh * GH + g;
+        const unsigned long long* src[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int sp = j < ns ? j : ns - 1;
+          src[4 * j] = p.part_ml + (row * ns + sp) * 2;
+          src[4 * j + 1] = src[4 * j] + 1;
+          src[4 * j + 2] = p.part_o + (row * ns + sp) * d + e;
+          src[4 * j + 3] = src[4 * j + 2] + 1;
+        }
+        uint32_t v[32];
+        poll_tagged<32>(src, v, tag, deadline, err);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j < ns) mx = fmaxf(mx, __uint_as_float(v[4 * j]));
+        float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j < ns) {
+            const float ms = __uint_as_float(v[4 * j]);
+            const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
+            l = fmaf(__uint_as_float(v[4 * j + 1]), f, l);
+            o0 = fmaf(__uint_as_float(v[4 * j + 2]), f, o0);
+            o1 = fmaf(__uint_as_float(v[4 * j + 3]), f, o1);
+          }
+        const uint32_t pair = f32_to_bf16_bits(__fdiv_rn(o0, l)) |
+                              (static_cast<uint32_t>(f32_to_bf16_bits(__fdiv_rn(o1, l))) << 16);
+        st_tagged(p.ctx + (b * k + (kvh * GH + g) * d + e) / 2, pair, tag);
+      }
+    } else {
       float* sw = sm_o;  // [GH][ns] weights exp(m_s - M); the o vectors are consumed
       __syncthreads();
       for (int it = threadIdx.x; it < GH * ns; it += kStepThreads) {
@@ -587,9 +632,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         cta_l[g] = l;
       }
       __syncthreads();
-      const int pairs = GH * static_cast<int>(d) / 2;
-      const int share = (pairs + ns - 1) / ns;
-      const int lo = split * share, hi = lo + share < pairs ? lo + share : pairs;
       for (int pi = lo + threadIdx.x; pi < hi; pi += kStepThreads) {
         const int g = (2 * pi) / static_cast<int>(d);
         const int64_t e = (2 * pi) % d;
@@ -628,17 +670,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     {
       const int pairs = static_cast<int>(nb * k / 2);
       uint32_t* xs2 = reinterpret_cast<uint32_t*>(x_stage);
-      for (int i0 = threadIdx.x; i0 < pairs; i0 += 4 * kStepThreads) {
-        const unsigned long long* src[4];
+      for (int i0 = threadIdx.x; i0 < pairs; i0 += 8 * kStepThreads) {  // one round trip per 2,048 pairs
+        const unsigned long long* src[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 8; ++j) {
           const int i = i0 + j * kStepThreads;
           src[j] = p.ctx + (i < pairs ? i : i0);
         }
-        uint32_t v[4];
-        poll_tagged<4>(src, v, tag, deadline, err);
+        uint32_t v[8];
+        poll_tagged<8>(src, v, tag, deadline, err);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < 8; ++j)
           if (i0 + j * kStepThreads < pairs) xs2[i0 + j * kStepThreads] = v[j];
       }
       __syncthreads();
