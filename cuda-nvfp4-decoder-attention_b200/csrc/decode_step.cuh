@@ -276,6 +276,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   uint32_t epoch;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(epoch) : "l"(sync + kSyncEpoch) : "memory");
   const uint32_t tag = epoch + 1u;
+  // Small inputs read late on the critical path (the projections' global
+  // scales, the per-head norm gains): loaded now, used microseconds later.
+  const float gamma_qkv = has_qkv ? __ldg(p.gamma[mat]) : 0.0f;
+  const float gamma_o = has_o ? __ldg(p.gamma[3]) : 0.0f;
+  uint32_t gq2[PPL], gk2[PPL];
+#pragma unroll
+  for (int j = 0; j < PPL; ++j) {
+    gq2[j] = has_attn ? __ldg(reinterpret_cast<const uint32_t*>(p.g_q) + lane + 32 * j) : 0u;
+    gk2[j] = has_attn ? __ldg(reinterpret_cast<const uint32_t*>(p.g_k) + lane + 32 * j) : 0u;
+  }
 
   // ---- the activation rows and the input-norm gain first: they head the
   // critical path, so their requests go out before any bulk traffic.
@@ -357,7 +367,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     else
       mma_gemv_pass_smem<false, 4>(qw_smem, qs_smem, x_stage, k, p.rq, p.rq, mrows, mred, outv);
     NVFP4DA_PHASE(13);
-    const float gamma = *p.gamma[mat];
+    const float gamma = gamma_qkv;
     const int rq2 = p.rq / 2;  // BF16 pairs (RQ and the row offsets are even)
     for (int i = threadIdx.x; i < rq2 * mrows; i += kStepThreads) {
       const int n = i / rq2, r = 2 * (i % rq2);
@@ -406,13 +416,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       }
       ss = warp_sum_f64(ss);
       const float inv = rms_inverse(static_cast<float>(ss), static_cast<float>(d), p.eps);
-      const uint32_t* g2 = reinterpret_cast<const uint32_t*>(is_q ? p.g_q : p.g_k);
       uint32_t* kdst =
           is_q ? nullptr : reinterpret_cast<uint32_t*>(p.k_cache + ((b * hkv + kvh) * p.capacity + pb) * d);
 #pragma unroll
       for (int j = 0; j < PPL; ++j) {
         const int pr = lane + 32 * j;
-        const uint32_t gg = g2[pr];
+        const uint32_t gg = is_q ? gq2[j] : gk2[j];
         const uint16_t n0 = f32_to_bf16_bits(
             __fmul_rn(__fmul_rn(__uint_as_float(pr2[j] << 16), inv), __uint_as_float(gg << 16)));
         const uint16_t n1 = f32_to_bf16_bits(
@@ -566,6 +575,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     // [j * share, j * share + share) of the GH x D context, every split's
     // partials for them in split order (the log-sum-exp combine of reference
     // decoder_attention.py's softmax).
+    NVFP4DA_PHASE(8);
     const int pairs = GH * static_cast<int>(d) / 2;
     const int share = (pairs + ns - 1) / ns;
     const int lo = split * share, hi = lo + share < pairs ? lo + share : pairs;
@@ -587,6 +597,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         }
         uint32_t v[32];
         poll_tagged<32>(src, v, tag, deadline, err);
+        NVFP4DA_PHASE(14);
         float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -694,7 +705,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                                   o_valid, mrows, mred, outv);
     else
       mma_gemv_pass_smem<false, 4>(ow_smem, os_smem, x_stage, k, p.o_tile_rows, o_valid, mrows, mred, outv);
-    const float gamma = *p.gamma[3];
+    const float gamma = gamma_o;
     for (int i = threadIdx.x; i < o_valid * mrows; i += kStepThreads) {
       const int n = i / o_valid, r = i % o_valid;
       const float v = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
