@@ -276,17 +276,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   uint32_t epoch;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(epoch) : "l"(sync + kSyncEpoch) : "memory");
   const uint32_t tag = epoch + 1u;
-  // Small inputs read late on the critical path (the projections' global
-  // scales, the per-head norm gains): loaded now, used microseconds later.
-  const float gamma_qkv = has_qkv ? __ldg(p.gamma[mat]) : 0.0f;
-  const float gamma_o = has_o ? __ldg(p.gamma[3]) : 0.0f;
-  uint32_t gq2[PPL], gk2[PPL];
-#pragma unroll
-  for (int j = 0; j < PPL; ++j) {
-    gq2[j] = has_attn ? __ldg(reinterpret_cast<const uint32_t*>(p.g_q) + lane + 32 * j) : 0u;
-    gk2[j] = has_attn ? __ldg(reinterpret_cast<const uint32_t*>(p.g_k) + lane + 32 * j) : 0u;
-  }
-
   // ---- the activation rows and the input-norm gain first: they head the
   // critical path, so their requests go out before any bulk traffic.
   constexpr int NCH = 2;
@@ -341,6 +330,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
   }
   NVFP4DA_PHASE(1);
+  // Small inputs read late on the critical path (the projections' global
+  // scales, the per-head norm gains): loaded now, used microseconds later.
+  const float gamma_qkv = has_qkv ? __ldg(p.gamma[mat]) : 0.0f;
+  const float gamma_o = has_o ? __ldg(p.gamma[3]) : 0.0f;
+  uint32_t gq2[PPL], gk2[PPL];
+#pragma unroll
+  for (int j = 0; j < PPL; ++j) {
+    gq2[j] = has_attn ? __ldg(reinterpret_cast<const uint32_t*>(p.g_q) + lane + 32 * j) : 0u;
+    gk2[j] = has_attn ? __ldg(reinterpret_cast<const uint32_t*>(p.g_k) + lane + 32 * j) : 0u;
+  }
+
 
   // ---- input RMSNorm of the activation rows -> MMA operand, QKV GEMV
   if (has_qkv) {
@@ -678,9 +678,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   // ---- O projection
   if (has_o) {
     // The context, as the splits publish it, into the BF16 operand rows.
+    bool o_f16;
     {
       const int pairs = static_cast<int>(nb * k / 2);
       uint32_t* xs2 = reinterpret_cast<uint32_t*>(x_stage);
+      float rmax = 0.0f;  // |x| maximum of this thread's pairs (used when B = 1)
       for (int i0 = threadIdx.x; i0 < pairs; i0 += 8 * kStepThreads) {  // one round trip per 2,048 pairs
         const unsigned long long* src[8];
 #pragma unroll
@@ -692,12 +694,47 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         poll_tagged<8>(src, v, tag, deadline, err);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          if (i0 + j * kStepThreads < pairs) xs2[i0 + j * kStepThreads] = v[j];
+          if (i0 + j * kStepThreads < pairs) {
+            xs2[i0 + j * kStepThreads] = v[j];
+            rmax = fmaxf(rmax, fmaxf(fabsf(__uint_as_float(v[j] << 16)), fabsf(__uint_as_float(v[j] & 0xffff0000u))));
+          }
       }
-      __syncthreads();
+      if (mrows == 1) {
+        // One row: the maximum from the polled values, then each thread
+        // converts its own pairs (the rule of mma_prepare_f16: row maximum to
+        // 2^14..2^15, exact or the BF16 path) -- one barrier instead of four.
+        rmax = warp_max_f32(rmax);
+        if (lane == 0) red_small[warp] = rmax;
+        __syncthreads();
+        float mx = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kStepWarps; ++w) mx = fmaxf(mx, red_small[w]);
+        int e = 0;
+        if (mx > 0.0f && isfinite(mx)) {
+          const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 127;  // floor(log2) for normals
+          e = 14 - (ex < -126 ? -126 : ex);
+          e = e > 126 ? 126 : (e < -126 ? -126 : e);
+        }
+        const float sc = __uint_as_float(static_cast<uint32_t>(127 + e) << 23);   // 2^e
+        const float isc = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e
+        uint32_t* x162 = reinterpret_cast<uint32_t*>(x16);
+        int inexact = 0;
+        for (int i = threadIdx.x; i < pairs; i += kStepThreads) {
+          const uint32_t w = xs2[i];
+          const float a = __uint_as_float(w << 16), c = __uint_as_float(w & 0xffff0000u);
+          const __half2 h = __floats2half2_rn(a * sc, c * sc);
+          inexact |= (__low2float(h) * isc != a) | (__high2float(h) * isc != c);  // round trip gives x back
+          x162[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        if (threadIdx.x == 0) escale[0] = isc;
+        o_f16 = __syncthreads_or(inexact) == 0;
+      } else {
+        __syncthreads();
+        o_f16 = mma_prepare_f16(x_stage, x16, k, mrows, escale, red_small);
+      }
     }
     NVFP4DA_PHASE(10);
-    const bool f16 = mma_prepare_f16(x_stage, x16, k, mrows, escale, red_small);
+    const bool f16 = o_f16;
     mbar_wait_bounded(&bar_o, 0, err);
     NVFP4DA_PHASE(11);
     if (f16)
