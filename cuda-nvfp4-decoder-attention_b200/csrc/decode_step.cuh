@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   __shared__ float escale[kMmaMaxM];
   __shared__ float red_small[kMmaMaxM * kStepWarps];
   __shared__ float outv[kStepMaxRows * 8];
-  __shared__ float sm_m[kStepWarps][GH], sm_l[kStepWarps][GH], wf[kStepWarps][GH], cta_m[GH], cta_l[GH];
+  __shared__ float sm_m[kStepWarps][GH], sm_l[kStepWarps][GH], cta_l[GH];
   __shared__ unsigned s_flag;
   [[maybe_unused]] constexpr unsigned kPhaseBase = 3072;
   constexpr int PPL = EPL / 2;  // RoPE pairs per lane (D = 32 * EPL)
@@ -544,32 +544,29 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 #pragma unroll
       for (int e = 0; e < EPL; ++e) sm_o[(warp * GH + g) * 32 * EPL + lane * EPL + e] = acc[g][e];
     __syncthreads();
-    if (threadIdx.x < GH) {
-      const int g = threadIdx.x;
+    // Every thread weighs the eight warps itself (the same arithmetic, in
+    // the same order, for every item of a head): no serial section and no
+    // second barrier.
+    const int di = static_cast<int>(d);
+    for (int idx = threadIdx.x; idx < GH * di; idx += kStepThreads) {
+      const int g = idx / di, e = idx % di;
       float mx = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kStepWarps; ++w) mx = fmaxf(mx, sm_m[w][g]);
-      float l = 0.0f;
+      float l = 0.0f, o = 0.0f;
 #pragma unroll
       for (int w = 0; w < kStepWarps; ++w) {
         const float f = (sm_m[w][g] == -INFINITY) ? 0.0f : expf(sm_m[w][g] - mx);
-        wf[w][g] = f;
         l = fmaf(sm_l[w][g], f, l);
+        o = fmaf(sm_o[(w * GH + g) * 32 * EPL + e], f, o);
       }
-      cta_m[g] = mx;
-      cta_l[g] = l;
-      unsigned long long* ml = p.part_ml + ((b * hq + kvh * GH + g) * ns + split) * 2;
-      st_tagged(ml, __float_as_uint(mx), tag);
-      st_tagged(ml + 1, __float_as_uint(l), tag);
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < GH * d; idx += kStepThreads) {
-      const int g = static_cast<int>(idx / d);
-      const int64_t e = idx % d;
-      float o = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kStepWarps; ++w) o = fmaf(sm_o[(w * GH + g) * 32 * EPL + e], wf[w][g], o);
-      st_tagged(p.part_o + ((b * hq + kvh * GH + g) * ns + split) * d + e, __float_as_uint(o), tag);
+      const int64_t row = b * hq + kvh * GH + g;
+      st_tagged(p.part_o + (row * ns + split) * d + e, __float_as_uint(o), tag);
+      if (e == 0) {
+        unsigned long long* ml = p.part_ml + (row * ns + split) * 2;
+        st_tagged(ml, __float_as_uint(mx), tag);
+        st_tagged(ml + 1, __float_as_uint(l), tag);
+      }
     }
     // The splits of (b, kv head) combine together: split j takes pairs
     // [j * share, j * share + share) of the GH x D context, every split's
