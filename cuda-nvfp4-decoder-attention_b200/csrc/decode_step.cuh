@@ -147,6 +147,26 @@ __device__ __forceinline__ void cta_wait(const unsigned* ctr, const int* idx, in
   __syncthreads();
 }
 
+// Wait for an mbarrier phase with the non-suspending test_wait, bounded by the
+// launch's deadline: a suspended try_wait can sleep past the phase flip, and
+// these waits sit on the critical path.
+__device__ __forceinline__ void mbar_spin_until(uint64_t* bar, uint32_t parity, unsigned long long deadline,
+                                                unsigned* err) {
+  for (uint32_t i = 0;; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return;
+    if ((i & 255u) == 255u && global_ns() > deadline) {
+      atomicOr(err, static_cast<unsigned>(kErrBarrierTimeout));
+      return;
+    }
+  }
+}
+
 // Tagged words: 32 bits of data (low) and the launch's tag (high).
 __device__ __forceinline__ void st_tagged(unsigned long long* p, uint32_t v, uint32_t tag) {
   const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | v;
@@ -258,7 +278,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   const int split = has_attn ? cta % ns : 0;
   const int64_t bh = has_attn ? cta / ns : 0;
-  const int64_t b = bh / hkv, kvh = bh % hkv;
+  const int64_t b = static_cast<int>(bh) / static_cast<int>(hkv), kvh = static_cast<int>(bh) % static_cast<int>(hkv);
   const int64_t pb = has_attn ? (p.past_lengths ? p.past_lengths[b] : p.past_length) : 0;
   const int64_t s0 = static_cast<int64_t>(split) * p.split_len;
   // Keys 0 .. P_b; never beyond the physical capacity, whatever a device-side
@@ -324,10 +344,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       bulk_g2s(qs_smem, p.scales[mat] + mat_row0 * ks, sb, &bar_qkv);
       bulk_g2s(qw_smem, p.packed[mat] + mat_row0 * kb, wb, &bar_qkv);
     }
-    if ((p.sched & 7) == 0 || !has_qkv) {
-      issue_kv();
-      issue_o();
-    }
+    if ((p.sched & 7) == 0 || (p.sched & 7) == 3 || !has_qkv) issue_kv();
+    if ((p.sched & 7) == 0 || !has_qkv) issue_o();
   }
   NVFP4DA_PHASE(1);
   // Small inputs read late on the critical path (the projections' global
@@ -346,10 +364,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   if (has_qkv) {
     bool f16 = prep_rows_regs<NCH, true>(p.x, k, mrows, gch, p.eps, x_stage, x16, escale, redf, redd, nullptr);
     NVFP4DA_PHASE(2);
-    mbar_wait_bounded(&bar_qkv, 0, err);
+    mbar_spin_until(&bar_qkv, 0, deadline, err);
     if (threadIdx.x == 0 && (p.sched & 7) != 0) {
-      issue_kv();
-      if ((p.sched & 7) == 1 || !has_attn) issue_o();
+      if ((p.sched & 7) != 3) issue_kv();
+      if ((p.sched & 7) == 1 || (p.sched & 7) == 3 || !has_attn) issue_o();
     }
     NVFP4DA_PHASE(3);
 #ifdef NVFP4DA_PHASES
@@ -447,7 +465,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         }
       }
     }
-    if (n_cache > 0) mbar_wait_bounded(&bar_kv, 0, err);
+    if (n_cache > 0) mbar_spin_until(&bar_kv, 0, deadline, err);
     __syncthreads();
     NVFP4DA_PHASE(6);
 
@@ -581,7 +599,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       // round trip once the slowest split has published.
       for (int pi = lo + threadIdx.x; pi < hi; pi += kStepThreads) {
         const int g = (2 * pi) / static_cast<int>(d);
-        const int64_t e = (2 * pi) % d;
+        const int64_t e = (2 * pi) % static_cast<int>(d);
         const int64_t row = b * hq + kvh * GH + g;
         const unsigned long long* src[32];
 #pragma unroll
@@ -642,7 +660,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       __syncthreads();
       for (int pi = lo + threadIdx.x; pi < hi; pi += kStepThreads) {
         const int g = (2 * pi) / static_cast<int>(d);
-        const int64_t e = (2 * pi) % d;
+        const int64_t e = (2 * pi) % static_cast<int>(d);
         const int64_t row = b * hq + kvh * GH + g;
         float o0 = 0.0f, o1 = 0.0f;
         for (int sp0 = 0; sp0 < ns; sp0 += 4) {
@@ -732,7 +750,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
     NVFP4DA_PHASE(10);
     const bool f16 = o_f16;
-    mbar_wait_bounded(&bar_o, 0, err);
+    mbar_spin_until(&bar_o, 0, deadline, err);
     NVFP4DA_PHASE(11);
     if (f16)
       mma_gemv_pass_smem<true, 4>(ow_smem, os_smem, reinterpret_cast<const uint16_t*>(x16), k, p.o_tile_rows,
