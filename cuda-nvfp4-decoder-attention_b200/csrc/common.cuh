@@ -30,7 +30,7 @@ enum DeviceError : unsigned {
 // clock64() at numbered points into a device table, read back by the debug
 // entry nvfp4da_debug_phases().  Compiled out of the normal library.
 #ifdef NVFP4DA_PHASES
-constexpr int kPhaseSlots = 16;
+constexpr int kPhaseSlots = 32;  // the last slot: clock64() at phase 0
 constexpr int kPhaseCtas = 4096;  // table rows; each kernel writes rows kPhaseBase + cta
 __device__ unsigned long long g_phase_table[kPhaseCtas * kPhaseSlots];
 #define NVFP4DA_PHASE(i)                                                                               \
@@ -40,7 +40,7 @@ __device__ unsigned long long g_phase_table[kPhaseCtas * kPhaseSlots];
       unsigned long long t_;                                                                           \
       if ((i) == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); else t_ = clock64();        \
       g_phase_table[cta_ * kPhaseSlots + (i)] = t_;                                                    \
-      if ((i) == 0) g_phase_table[cta_ * kPhaseSlots + 15] = clock64();                                \
+      if ((i) == 0) g_phase_table[cta_ * kPhaseSlots + kPhaseSlots - 1] = clock64();                                \
     }                                                                                                  \
   } while (0)
 #else

@@ -86,9 +86,7 @@ struct StepParams {
   size_t tag_words;             // the region's size, cleared when the epoch wraps
   unsigned* sync;    // slot
   unsigned long long timeout_ns;
-  // When the K/V tile and the O rows are requested: 0 at launch, 1 once the
-  // QKV rows have landed, 2 the K/V tile then and the O rows after the
-  // attention unit.
+  // When the K/V tile and the O rows are requested (see the kernel).
   int sched;
   // dynamic shared-memory layout (byte offsets); qs/qw/kv/q and comb overlay
   uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
@@ -321,6 +319,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   // rows now, the K/V tile and the O rows later (p.sched), so that they do
   // not queue ahead of the critical path.
   const int64_t ks = k / 16, kb = k / 2;
+  // p.sched & 7: 0 K/V tile and O rows at launch; 1 both once the QKV rows
+  // have landed; 2 the K/V tile then, the O rows after the attention unit
+  // (at once where a CTA has none); 3 the K/V tile at launch, the O rows once
+  // the QKV rows have landed; 4 the K/V tile at launch, the O rows as in 2.
+  const int sched = p.sched & 7;
+  const bool kv_at_launch = sched == 0 || sched == 3 || sched == 4;
+  const int o_when = sched == 0 ? 0 : (sched == 2 || sched == 4 ? 2 : 1);
   auto issue_kv = [&]() {
     if (n_cache > 0) {
       const uint32_t tb = static_cast<uint32_t>(n_cache * d * 2);
@@ -344,8 +349,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       bulk_g2s(qs_smem, p.scales[mat] + mat_row0 * ks, sb, &bar_qkv);
       bulk_g2s(qw_smem, p.packed[mat] + mat_row0 * kb, wb, &bar_qkv);
     }
-    if ((p.sched & 7) == 0 || (p.sched & 7) == 3 || !has_qkv) issue_kv();
-    if ((p.sched & 7) == 0 || !has_qkv) issue_o();
+    if (kv_at_launch || !has_qkv) issue_kv();
+    if (o_when == 0 || !has_qkv) issue_o();
   }
   NVFP4DA_PHASE(1);
   // Small inputs read late on the critical path (the projections' global
@@ -365,9 +370,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     bool f16 = prep_rows_regs<NCH, true>(p.x, k, mrows, gch, p.eps, x_stage, x16, escale, redf, redd, nullptr);
     NVFP4DA_PHASE(2);
     mbar_spin_until(&bar_qkv, 0, deadline, err);
-    if (threadIdx.x == 0 && (p.sched & 7) != 0) {
-      if ((p.sched & 7) != 3) issue_kv();
-      if ((p.sched & 7) == 1 || (p.sched & 7) == 3 || !has_attn) issue_o();
+    if (threadIdx.x == 0) {
+      if (!kv_at_launch) issue_kv();
+      if (o_when == 1 || (o_when == 2 && !has_attn)) issue_o();
     }
     NVFP4DA_PHASE(3);
 #ifdef NVFP4DA_PHASES
@@ -465,6 +470,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         }
       }
     }
+    NVFP4DA_PHASE(18);
     if (n_cache > 0) mbar_spin_until(&bar_kv, 0, deadline, err);
     __syncthreads();
     NVFP4DA_PHASE(6);
@@ -549,6 +555,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     // ---- combine the eight warps (their o vectors reuse the K/V tile) and
     // leave this split's (m, l, o) in the workspace
     __syncthreads();  // every warp is done with the tile
+    NVFP4DA_PHASE(16);
     float* sm_o = reinterpret_cast<float*>(smem + p.off_kv);  // [warps][GH][D]
     if (lane == 0) {
 #pragma unroll
@@ -686,7 +693,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         st_tagged(p.ctx + (b * k + (kvh * GH + g) * d + e) / 2, pair, tag);
       }
     }
-    if (threadIdx.x == 0 && (p.sched & 7) == 2 && has_qkv) issue_o();
+    if (threadIdx.x == 0 && o_when == 2 && has_qkv) issue_o();
     NVFP4DA_PHASE(9);
   }
 
@@ -714,6 +721,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             rmax = fmaxf(rmax, fmaxf(fabsf(__uint_as_float(v[j] << 16)), fabsf(__uint_as_float(v[j] & 0xffff0000u))));
           }
       }
+      NVFP4DA_PHASE(17);
       if (mrows == 1) {
         // One row: the maximum from the polled values, then each thread
         // converts its own pairs (the rule of mma_prepare_f16: row maximum to
