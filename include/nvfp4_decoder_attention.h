@@ -168,10 +168,11 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* wo
  * differs).  The one-kernel step covers T == 1, B <= 8, hidden % 256 == 0,
  * hidden <= 4096, head_dim in {64, 128, 256}, 1/2/4/8 query heads per KV head,
  * no stage outputs, and a K/V tile per split that fits in shared memory.  It
- * is a cooperative launch whose phases are ordered by counters in a
- * library-owned slot of the stream it is launched on (64 slots per device):
- * a graph that captured it must not be replayed concurrently with other
- * forwards issued to the capturing stream.  No counterpart in the reference
+ * is a cooperative launch whose phases hand data to one another through a
+ * library-owned region of the stream it is launched on (64 slots of 512 KB
+ * per device; configurations whose hand-off words do not fit take the
+ * chain): a graph that captured it must not be replayed concurrently with
+ * other forwards issued to the capturing stream.  No counterpart in the reference
  * (its forward is always the modular chain). */
 #define NVFP4DA_PATH_AUTO 0
 #define NVFP4DA_PATH_CHAIN 1
