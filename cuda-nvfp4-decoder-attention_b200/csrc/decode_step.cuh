@@ -273,6 +273,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   const int64_t qrow0 = static_cast<int64_t>(cta) * p.rq;  // concatenated QKV row
   const int mat = qrow0 < hq * d ? 0 : (qrow0 < (hq + hkv) * d ? 1 : 2);
   const int64_t mat_row0 = qrow0 - (mat == 0 ? 0 : (mat == 1 ? hq * d : (hq + hkv) * d));
+  const int64_t ks = k / 16, kb = k / 2;
+  // The QKV slice heads the critical path: thread 0 requests it before
+  // anything else (the barrier below publishes the initialised mbarriers to
+  // the other threads before they wait on them).
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_qkv, 1);
+    mbar_init(&bar_kv, 1);
+    mbar_init(&bar_o, 1);
+    fence_mbar_init();
+    if (has_qkv) {
+      const uint32_t sb = static_cast<uint32_t>(p.rq * ks), wb = static_cast<uint32_t>(p.rq * kb);
+      mbar_arrive_expect_tx(&bar_qkv, sb + wb);
+      bulk_g2s(qs_smem, p.scales[mat] + mat_row0 * ks, sb, &bar_qkv);
+      bulk_g2s(qw_smem, p.packed[mat] + mat_row0 * kb, wb, &bar_qkv);
+    }
+  }
 
   const int split = has_attn ? cta % ns : 0;
   const int64_t bh = has_attn ? cta / ns : 0;
@@ -306,19 +322,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       for (int m = 0; m < mrows; ++m) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + m * k + 8 * idx));
   }
 
-  if (threadIdx.x == 0) {
-    mbar_init(&bar_qkv, 1);
-    mbar_init(&bar_kv, 1);
-    mbar_init(&bar_o, 1);
-    fence_mbar_init();
-  }
   __syncthreads();
   const unsigned long long deadline = global_ns() + p.timeout_ns;
 
   // ---- input slices of this CTA (none is written by the step): the QKV
   // rows now, the K/V tile and the O rows later (p.sched), so that they do
   // not queue ahead of the critical path.
-  const int64_t ks = k / 16, kb = k / 2;
   // p.sched & 7: 0 K/V tile and O rows at launch; 1 both once the QKV rows
   // have landed; 2 the K/V tile then, the O rows after the attention unit
   // (at once where a CTA has none); 3 the K/V tile at launch, the O rows once
@@ -343,12 +352,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
   };
   if (threadIdx.x == 0) {
-    if (has_qkv) {
-      const uint32_t sb = static_cast<uint32_t>(p.rq * ks), wb = static_cast<uint32_t>(p.rq * kb);
-      mbar_arrive_expect_tx(&bar_qkv, sb + wb);
-      bulk_g2s(qs_smem, p.scales[mat] + mat_row0 * ks, sb, &bar_qkv);
-      bulk_g2s(qw_smem, p.packed[mat] + mat_row0 * kb, wb, &bar_qkv);
-    }
     if (kv_at_launch || !has_qkv) issue_kv();
     if (o_when == 0 || !has_qkv) issue_o();
   }
