@@ -572,34 +572,36 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 #pragma unroll
       for (int e = 0; e < EPL; ++e) sm_o[(warp * GH + g) * 32 * EPL + lane * EPL + e] = acc[g][e];
     __syncthreads();
-    // Every thread weighs the eight warps itself (the same arithmetic, in
-    // the same order, for every item of a head): no serial section and no
-    // second barrier.
+    // One thread per (head, warp) computes that warp's weight exp(m_w - M);
+    // then every item is an 8-term FMA chain in warp order, and one thread per
+    // head publishes (M, l).
+    float* wsm = reinterpret_cast<float*>(outv);  // [GH][warps], free until the O pass
+    if (threadIdx.x < GH * kStepWarps) {
+      const int g = threadIdx.x / kStepWarps, w = threadIdx.x % kStepWarps;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kStepWarps; ++u) mx = fmaxf(mx, sm_m[u][g]);
+      wsm[threadIdx.x] = (sm_m[w][g] == -INFINITY) ? 0.0f : expf(sm_m[w][g] - mx);
+      if (w == 0) cta_l[g] = mx;
+    }
+    __syncthreads();
     const int di = static_cast<int>(d);
     for (int idx = threadIdx.x; idx < GH * di; idx += kStepThreads) {
       const int g = idx / di, e = idx % di;
-      float mx = -INFINITY;
+      float o = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kStepWarps; ++w) mx = fmaxf(mx, sm_m[w][g]);
-      float l = 0.0f, o = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kStepWarps; ++w) {
-        const float f = (sm_m[w][g] == -INFINITY) ? 0.0f : expf(sm_m[w][g] - mx);
-        l = fmaf(sm_l[w][g], f, l);
-        o = fmaf(sm_o[(w * GH + g) * 32 * EPL + e], f, o);
-      }
+      for (int w = 0; w < kStepWarps; ++w) o = fmaf(sm_o[(w * GH + g) * 32 * EPL + e], wsm[g * kStepWarps + w], o);
       const int64_t row = b * hq + kvh * GH + g;
       st_tagged(p.part_o + (row * ns + split) * d + e, __float_as_uint(o), tag);
       if (e == 0) {
+        float l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kStepWarps; ++w) l = fmaf(sm_l[w][g], wsm[g * kStepWarps + w], l);
         unsigned long long* ml = p.part_ml + (row * ns + split) * 2;
-        st_tagged(ml, __float_as_uint(mx), tag);
+        st_tagged(ml, __float_as_uint(cta_l[g]), tag);
         st_tagged(ml + 1, __float_as_uint(l), tag);
       }
     }
-    // The splits of (b, kv head) combine together: split j takes pairs
-    // [j * share, j * share + share) of the GH x D context, every split's
-    // partials for them in split order (the log-sum-exp combine of reference
-    // decoder_attention.py's softmax).
     NVFP4DA_PHASE(8);
     const int pairs = GH * static_cast<int>(d) / 2;
     const int share = (pairs + ns - 1) / ns;
