@@ -17,6 +17,7 @@
 
 #include "../../include/nvfp4_decoder_attention.h"
 #include "attention.cuh"
+#include "attention_stream.cuh"
 #include "attention_prefill.cuh"
 #include "elementwise.cuh"
 #include "gemv_kernel.cuh"
@@ -312,14 +313,36 @@ int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t*
 }
 
 // ---------------------------------------------------------------- attention plan
+// Two decode-attention kernels share one workspace layout (the partials at
+// the start, the counter words at partial_bytes, both sized for the larger of
+// the two plans), so a call planned for one can run the other:
+//  * attn_split_kernel: splits of a fixed length, CUDA-core loop from global
+//    memory, cluster (DSMEM) combine up to 16 splits -- lowest latency for
+//    short caches;
+//  * attn_stream_kernel: one persistent CTA per SM over the flattened tile
+//    line of all (sequence, KV head) pairs, TMA-fed tensor-core loop -- HBM
+//    rate for long caches (visible length >= kStreamMinVisible).
 struct AttnPlan {
   int epl, gh, head_groups, splits;
   int64_t split_len;
   bool cluster;  // splits combine through DSMEM as one cluster (2..16 splits)
+  bool stream;   // attn_stream_kernel applies (it is still skipped for unaligned or huge caches)
+  int stream_grid;
+  uint32_t stream_smem;
   size_t partial_bytes, counter_bytes;
 };
 
 constexpr int kMaxAttnCluster = 16;
+constexpr int64_t kStreamMinVisible = 2048;
+
+uint32_t stream_smem_bytes(int64_t head_dim, int64_t batch) {
+  switch (head_dim) {
+    case 64: return AsCfg<64>::bytes(static_cast<int>(batch));
+    case 128: return AsCfg<128>::bytes(static_cast<int>(batch));
+    case 256: return AsCfg<256>::bytes(static_cast<int>(batch));
+    default: return 0;
+  }
+}
 
 bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                     int64_t max_past, AttnPlan& pl) {
@@ -357,9 +380,73 @@ bool plan_attention(int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_h
   pl.split_len = split_len;
   pl.cluster = splits > 1 && splits <= kMaxAttnCluster;
   const bool global = splits > 1 && !pl.cluster;
-  pl.partial_bytes =
-      global ? align_up(static_cast<size_t>(batch * tokens * q_heads) * splits * (head_dim + 2) * 4, 256) : 0;
-  pl.counter_bytes = global ? align_up(static_cast<size_t>(base) * 4, 256) : 0;
+  size_t part = global ? static_cast<size_t>(batch * tokens * q_heads) * splits * (head_dim + 2) * 4 : 0;
+  size_t words = global ? static_cast<size_t>(base) : 0;
+  // The streaming kernel: group * T query rows per KV head fit one 8-wide MMA
+  // tile, and the per-sequence prefix fits its shared memory.
+  pl.stream_smem = stream_smem_bytes(head_dim, batch);
+  pl.stream = visible >= kStreamMinVisible && group * tokens <= kAsRows && batch <= kAsMaxBatch &&
+              pl.stream_smem > 0 && pl.stream_smem <= kMaxDynSmem && tensor_map_encoder() != nullptr;
+  pl.stream_grid = sm_count();
+  if (pl.stream) {
+    const int64_t pairs = batch * kv_heads;
+    part = std::max(part, static_cast<size_t>(pairs + pl.stream_grid) * kAsRows * (head_dim + 2) * 4);
+    words = std::max(words, static_cast<size_t>(pairs) + 1);  // counters + the error word
+  }
+  pl.partial_bytes = align_up(part, 256);
+  pl.counter_bytes = align_up(words * 4, 256);
+  return true;
+}
+
+template <int D>
+cudaError_t launch_stream_t(const CUtensorMap& tk, const CUtensorMap& tv, const StreamAttnParams& p, int grid,
+                            uint32_t smem, cudaStream_t s, bool pdl) {
+  auto* k = attn_stream_kernel<D>;
+  cudaError_t e = ensure_smem(k, smem);
+  if (e != cudaSuccess) return e;
+  return launch(k, dim3(static_cast<unsigned>(grid)), dim3(kAsThreads), smem, s, pdl, tk, tv, p);
+}
+
+// Run attn_stream_kernel if the call allows it (returns false, launching
+// nothing, otherwise); *launch_err is set if the launch itself failed.
+bool try_stream_attention(const AttnPlan& pl, const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                          uint16_t* ctx, int64_t batch, int64_t tokens, int64_t q_heads, int64_t kv_heads,
+                          int64_t capacity, int64_t head_dim, int64_t past_length, const int64_t* past_lengths,
+                          void* ws, cudaStream_t s, bool pdl, int64_t pos_offset, float* out_partial,
+                          cudaError_t* launch_err) {
+  *launch_err = cudaSuccess;
+  if (!pl.stream || !ws) return false;
+  const int64_t rows = batch * kv_heads * capacity;
+  if (rows >= (int64_t(1) << 31) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(q, 4)) return false;
+  CUtensorMap tk, tv;
+  if (!make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kc, head_dim, rows, head_dim * 2, 64, kAsTile,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, vc, head_dim, rows, head_dim * 2, 64, kAsTile,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return false;
+  StreamAttnParams p{};
+  p.q = q;
+  p.ctx = ctx;
+  p.out_partial = out_partial;
+  p.batch = static_cast<int>(batch);
+  p.tokens = static_cast<int>(tokens);
+  p.q_heads = static_cast<int>(q_heads);
+  p.kv_heads = static_cast<int>(kv_heads);
+  p.group = static_cast<int>(q_heads / kv_heads);
+  p.capacity = capacity;
+  p.past_length = past_length;
+  p.past_lengths = past_lengths;
+  p.pos_offset = pos_offset;
+  p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)));
+  p.partials = static_cast<float*>(ws);
+  p.counters = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pl.partial_bytes);
+  p.err = p.counters + batch * kv_heads;
+  p.pdl = pdl ? 1 : 0;
+  switch (head_dim) {
+    case 64: *launch_err = launch_stream_t<64>(tk, tv, p, pl.stream_grid, pl.stream_smem, s, pdl); break;
+    case 128: *launch_err = launch_stream_t<128>(tk, tv, p, pl.stream_grid, pl.stream_smem, s, pdl); break;
+    default: *launch_err = launch_stream_t<256>(tk, tv, p, pl.stream_grid, pl.stream_smem, s, pdl); break;
+  }
   return true;
 }
 
@@ -443,6 +530,18 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
   if (pl.partial_bytes + pl.counter_bytes > ws_bytes || (pl.partial_bytes > 0 && !ws))
     return fail(NVFP4DA_ERR_WORKSPACE, "attention workspace too small (%zu < %zu bytes)", ws_bytes,
                 pl.partial_bytes + pl.counter_bytes);
+  if (pl.stream && clear_counters) {
+    cudaError_t e = cudaMemsetAsync(static_cast<char*>(ws) + pl.partial_bytes, 0, pl.counter_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "attention counter clear");
+  }
+  {
+    cudaError_t le;
+    if (try_stream_attention(pl, q, kc, vc, ctx, batch, tokens, q_heads, kv_heads, capacity, head_dim, past_length,
+                             past_lengths, ws, s, pdl, pos_offset, out_partial, &le)) {
+      if (le != cudaSuccess) return cuda_fail(le, "streaming attention launch");
+      return NVFP4DA_OK;
+    }
+  }
   AttnParams p{};
   p.q = q;
   p.k_cache = kc;
@@ -460,14 +559,14 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
   p.splits = pl.splits;
   p.head_groups = pl.head_groups;
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)));
-  const bool global = pl.partial_bytes > 0;
+  const bool global = pl.splits > 1 && !pl.cluster;
   p.partials = global ? static_cast<float*>(ws) : nullptr;
   p.counters = global ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pl.partial_bytes) : nullptr;
   p.pdl = pdl ? 1 : 0;
   p.cluster_combine = pl.cluster ? 1 : 0;
   p.pos_offset = pos_offset;
   p.out_partial = out_partial;
-  if (clear_counters && global) {
+  if (clear_counters && global && !pl.stream) {
     cudaError_t e = cudaMemsetAsync(p.counters, 0, pl.counter_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "attention counter clear");
   }
