@@ -15,6 +15,13 @@ Multi-GPU (torchrun, one process per GPU): every rank decodes its own
 independent sequence (weak scaling, no collective on the data path); value is
 the tokens of all ranks over the max-over-ranks device time.
 
+The line also carries `workloads`, the other configs measured in the same run
+at the same N: configs[2] batch-sharded (B=64 split into 64/N sequences per
+rank, device-side past lengths, no collective), configs[3] KV-length-sharded
+(32768/N cache positions per rank, NCCL all-gather of the log-sum-exp
+partials) and configs[4] prefill (replicated per rank), each with per-GPU HBM
+GB/s or TFLOP/s against the measured peaks.
+
 --impl reference times the reference's CPU path (the numpy restatement of
 reference/decoder_attention_nvfp4.py in oracle/; the Python reference itself
 cannot travel to the GPU box) on the host cores, on the same workload.
@@ -332,7 +339,19 @@ def run_gpu(args) -> None:
                      "step_bytes": nbytes["step"]})
 
     # ---- end to end through the drop-in Python API with host buffers
+    step_supported = reps[0].fw.step_supported
     e2e = run_e2e(args, reps, decoder_attention_cuda, stream, world)
+
+    # ---- the other configs: batch-sharded configs[2], KV-sharded configs[3], prefill configs[4]
+    workloads = {}
+    if not args.skip_workloads:
+        del reps
+        torch.cuda.empty_cache()
+        for name, fn in (("c2_batch_sharded", lambda: run_c2_batch_sharded(capi, world, rank, stream, peak)),
+                         ("c3_kv_sharded", lambda: run_c3_kv_sharded(capi, world, rank, stream, peak)),
+                         ("c4_prefill", lambda: run_c4_prefill(capi, world, rank, stream))):
+            workloads[name] = fn()
+            torch.cuda.empty_cache()
 
     if rank != 0:
         _finish(world)
@@ -351,13 +370,218 @@ def run_gpu(args) -> None:
         "kernels": kernels,
         "paths_us_per_step": {n: round(v * 1e3 / (reps_k * n_rep), 3) for n, v in path_ms.items()},
         "e2e": e2e,
-        "gpu_launches": (1 if reps[0].fw.step_supported else 3) * k,
+        "workloads": workloads,
+        "gpu_launches": (1 if step_supported else 3) * k,
         "clocks": clk,
     }
     if world == 1 and not args.skip_cpu:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     print(json.dumps(line), flush=True)
     _finish(world)
+
+
+# ---------------------------------------------------------------- sharded workloads (sub-objects of the line)
+def _quantized_weights(inp, capi):
+    from nvfp4_tensor import NVFP4Tensor
+
+    ws = {}
+    for k, w in inp.weights_fp32.items():
+        packed, scales, gamma = capi.quantize(w.cuda())
+        ws[k] = NVFP4Tensor(packed, scales, gamma, tuple(w.shape))
+    return ws
+
+
+def _weight_bytes(h: int, kvw: int) -> int:
+    w = lambda n, k: n * (k // 2 + k // 16) + 4  # noqa: E731
+    return 2 * w(h, h) + 2 * w(kvw, h)
+
+
+def _time_steps(fn, steps: int, warmup: int, stream, world: int, graph_ok: bool = True):
+    """Device ms of `steps` calls of fn (replays of a CUDA graph of one call
+    when graph_ok and it captures, else eager), max over ranks; and whether a
+    graph was used."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.synchronize()
+    graph = None
+    if graph_ok:
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                fn()
+            graph = g
+        except Exception:
+            torch.cuda.synchronize()
+            graph = None
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                fn()
+        end.record(stream)
+    end.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(end), world), graph is not None
+
+
+def run_c2_batch_sharded(capi, world, rank, stream, peak, steps=50) -> dict:
+    """B=64, P_b ~ U[1024, 8191] (seeded), C=8192; the 64
+    sequences split into contiguous groups of 64/N, one per rank, each rank
+    running the forward on its own group with device-side past lengths (no
+    collective on the data path)."""
+    import synthetic
+
+    full = synthetic.batched_shape()
+    if full.batch % world:
+        return {"skipped": f"B=64 does not split over {world} ranks"}
+    per = full.batch // world
+    pasts = full.past_lengths[rank * per:(rank + 1) * per]
+    shape = synthetic.DecodeShape(batch=per, capacity=full.capacity, past_lengths=tuple(pasts))
+    inp = synthetic.make_decode_inputs(shape, seed=2 + rank, cache_device="cuda")
+    ws = _quantized_weights(inp, capi)
+    h, kvw = shape.hidden, shape.kv_width
+    kv_read = sum((p + 1) * 2 * kvw * 2 for p in pasts)
+    bytes_rank = _weight_bytes(h, kvw) + kv_read + per * 2 * kvw * 2 + 2 * per * h * 2
+    # Rotate cache replicas so that one step's traffic stays above 2 x L2.
+    n_rep = max(1, math.ceil(2 * L2_BYTES / bytes_rank))
+    x, g_in = inp.x.cuda(), inp.input_norm_weight.cuda()
+    g_q, g_k = inp.q_norm_weight.cuda(), inp.k_norm_weight.cuda()
+    pl = torch.tensor(pasts, dtype=torch.int64, device="cuda")
+    fws = []
+    for r in range(n_rep):
+        kc = inp.k_cache if r == 0 else inp.k_cache.clone()
+        vc = inp.v_cache if r == 0 else inp.v_cache.clone()
+        out = torch.empty_like(x)
+        fws.append(capi.Forward(x, g_in, ws["q"], ws["k"], ws["v"], g_q, g_k, ws["o"], kc, vc, out, past_length=0,
+                                past_lengths=pl, max_past_length=max(pasts)))
+
+    def step_all():
+        for fw in fws:
+            fw.run(stream)
+
+    reps = max(1, steps // n_rep)
+    ms, graphed = _time_steps(step_all, reps, 3, stream, world)
+    ms_step = ms / (reps * n_rep)
+    # bytes of the slowest rank bound the step; report this rank's and the job's
+    gbs = bytes_rank / (ms_step * 1e-3) / 1e9
+    tot = torch.tensor([float(bytes_rank)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(tot)
+    return {"config": "configs[2]: B=64 T=1 P_b~U[1024,8191] seed 2024 C=8192, batch-sharded "
+                      f"{per} sequences per rank", "ranks": world,
+            "tokens_per_s": round(full.batch / (ms_step * 1e-3), 1), "ms_per_step": round(ms_step, 5),
+            "hbm_gbs_per_gpu": round(gbs, 1), "frac_per_gpu": round(gbs / peak, 4),
+            "bytes_per_step_job": int(tot.item()), "bytes_per_step_rank0": bytes_rank,
+            "path": "fused QKV + streaming split-KV attention + O GEMV (3 PDL-chained launches per rank)",
+            "replicas": n_rep, "graph": graphed, "steps": reps * n_rep}
+
+
+def run_c3_kv_sharded(capi, world, rank, stream, peak, steps=30) -> dict:
+    """B=8, P=32767, C=32768; the KV length split into N
+    contiguous shards, one per rank: replicated projections, per-shard
+    log-sum-exp partials, NCCL all-gather of the partials, combine, O."""
+    import synthetic
+    from kv_sharding import ShardedDecoderAttention
+
+    full = synthetic.LONG_CONTEXT
+    sda = ShardedDecoderAttention(full.capacity, group=None)
+    shard = sda.shard
+    shape = synthetic.DecodeShape(batch=full.batch, capacity=shard.capacity, past_lengths=full.past_lengths)
+    inp = synthetic.make_decode_inputs(shape, seed=3 + rank, cache_device="cuda")
+    ws = _quantized_weights(inp, capi)
+    x, g_in = inp.x.cuda(), inp.input_norm_weight.cuda()
+    g_q, g_k = inp.q_norm_weight.cuda(), inp.k_norm_weight.cuda()
+    past = full.past_lengths[0]
+    h, kvw, b = shape.hidden, shape.kv_width, shape.batch
+    visible = max(0, min(shard.capacity, past + 1 - shard.start))
+    gather = world * b * shape.q_heads * (shape.head_dim + 2) * 4
+    bytes_rank = _weight_bytes(h, kvw) + b * visible * 2 * kvw * 2 + 2 * b * h * 2 + gather
+
+    def step():
+        sda.forward_(x, g_in, ws["q"], ws["k"], ws["v"], g_q, g_k, ws["o"], inp.k_cache, inp.v_cache, past)
+
+    # Eager at N > 1 (the step holds an NCCL collective); a graph of 4 steps at N = 1.
+    ms, graphed = _time_steps(lambda: [step() for _ in range(4)], max(1, steps // 4), 3, stream, world,
+                              graph_ok=world == 1)
+    ms_step = ms / (4 * max(1, steps // 4))
+    # the all-gather alone (same partial size), for its share of the step
+    ag_share = None
+    if world > 1:
+        import torch.distributed as dist
+
+        part = torch.zeros((b * shape.q_heads, shape.head_dim + 2), dtype=torch.float32, device="cuda")
+        flat = torch.empty((world * part.shape[0], part.shape[1]), dtype=torch.float32, device="cuda")
+        ag_ms, _ = _time_steps(lambda: dist.all_gather_into_tensor(flat, part), 50, 3, stream, world,
+                               graph_ok=False)
+        ag_share = round((ag_ms / 50) / ms_step, 4)
+    gbs = bytes_rank / (ms_step * 1e-3) / 1e9
+    return {"config": f"configs[3]: B=8 T=1 P=32767 C=32768, KV length sharded {shard.capacity} positions per rank",
+            "ranks": world, "tokens_per_s": round(b / (ms_step * 1e-3), 1), "ms_per_step": round(ms_step, 5),
+            "hbm_gbs_per_gpu": round(gbs, 1), "frac_per_gpu": round(gbs / peak, 4),
+            "bytes_per_step_rank0": bytes_rank, "allgather_share_of_step": ag_share,
+            "path": "fused front half (shard append) + streaming attention partials + NCCL all-gather "
+                    "+ combine + O GEMV", "graph": graphed, "steps": 4 * max(1, steps // 4)}
+
+
+def run_c4_prefill(capi, world, rank, stream, steps=10) -> dict:
+    """B=4, T=2048, P=0, C=4096 on every rank (replicas: the
+    prefill batch does not shard in this design).  Tensor roofline on the
+    GEMM and the causal attention."""
+    import synthetic
+
+    shape = synthetic.PREFILL
+    inp = synthetic.make_decode_inputs(shape, seed=4, cache_device="cuda")
+    ws = _quantized_weights(inp, capi)
+    x = inp.x.cuda()
+    out = torch.empty_like(x)
+    fw = capi.Forward(x, inp.input_norm_weight.cuda(), ws["q"], ws["k"], ws["v"], inp.q_norm_weight.cuda(),
+                      inp.k_norm_weight.cuda(), ws["o"], inp.k_cache, inp.v_cache, out, past_length=0)
+    m, h, kvw = shape.batch * shape.tokens, shape.hidden, shape.kv_width
+    ms, _ = _time_steps(lambda: fw.run(stream), steps, 3, stream, world)
+    ms_step = ms / steps
+    xin = torch.randn((m, h), device="cuda").to(torch.bfloat16)
+    y = torch.empty((m, h), dtype=torch.bfloat16, device="cuda")
+    g_ms, _ = _time_steps(lambda: capi.w4a16_gemm(xin, ws["q"], y, stream), steps, 3, stream, world)
+    lib = capi.load()
+    q = torch.randn((shape.batch, shape.tokens, shape.q_heads, shape.head_dim), device="cuda").to(torch.bfloat16)
+    ctx = torch.empty_like(q)
+    wsb = lib.nvfp4da_gqa_attention_workspace_size(shape.batch, shape.tokens, shape.q_heads, shape.kv_heads,
+                                                   shape.head_dim, 0)
+    aws = torch.empty(max(wsb, 256), dtype=torch.uint8, device="cuda")
+
+    def attn():
+        st = lib.nvfp4da_gqa_attention_cached(q.data_ptr(), inp.k_cache.data_ptr(), inp.v_cache.data_ptr(),
+                                              ctx.data_ptr(), shape.batch, shape.tokens, shape.q_heads,
+                                              shape.kv_heads, shape.capacity, shape.head_dim, 0, None, 0,
+                                              aws.data_ptr(), wsb, stream.cuda_stream)
+        assert st == 0, lib.nvfp4da_last_error()
+
+    a_ms, _ = _time_steps(attn, steps, 3, stream, world)
+    try:
+        peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+        src = "measured (MEASURED_PEAKS.json bf16_tflops)"
+    except Exception:
+        peak, src = 1590.0, "fallback 1.59 PFLOP/s"
+    gemm_fl = 2.0 * m * h * h
+    attn_fl = 2.0 * 2.0 * shape.batch * shape.q_heads * (shape.tokens * (shape.tokens + 1) / 2) * shape.head_dim
+    step_fl = 2.0 * m * h * (2 * h + 2 * kvw) + attn_fl
+    g_tf = gemm_fl / (g_ms / steps * 1e-3) / 1e12
+    a_tf = attn_fl / (a_ms / steps * 1e-3) / 1e12
+    return {"config": "configs[4]: B=4 T=2048 P=0 C=4096 (replicated per rank)", "ranks": world,
+            "tokens_per_s": round(world * m / (ms_step * 1e-3), 1), "ms_per_step": round(ms_step, 4),
+            "step_tflops": round(step_fl / (ms_step * 1e-3) / 1e12, 1),
+            "gemm_q_tflops": round(g_tf, 1), "gemm_frac": round(g_tf / peak, 4),
+            "attention_tflops": round(a_tf, 1), "attention_frac": round(a_tf / peak, 4),
+            "attention_ms": round(a_ms / steps, 4), "peak_tflops": peak, "peak_source": src,
+            "flops_note": "attention counts the causal half: 4*B*Hq*D*T(T+1)/2"}
 
 
 def run_prefill(args) -> None:
@@ -541,6 +765,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-workloads", action="store_true",
+                    help="only the configs[0] line (no configs[2]/[3]/[4] sub-objects)")
     ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
                     help="decode = configs[0] (the metric's workload); prefill = configs[4], reported separately")
     args = ap.parse_args()

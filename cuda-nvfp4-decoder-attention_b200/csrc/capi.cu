@@ -803,13 +803,30 @@ unsigned* slot_base_for_device(int dev) {
 
 // The slot of `stream` on the current device (assigned on first use), or
 // nullptr when every slot is taken; *tagged (if given) = the slot's hand-off
-// region.
+// region.  Slots are never released, so a (device, stream) -> slot answer
+// stays valid for the life of the process: each host thread keeps its last
+// answer and repeats it without the lock or the map lookup.  (A device reset
+// after the first call is not supported: the addresses would be stale.)
+struct SlotHit {
+  int dev = -1;
+  uintptr_t stream = 0;
+  unsigned* slot = nullptr;
+  unsigned long long* tagged = nullptr;
+};
+thread_local SlotHit tl_slot_hit;
+
 unsigned* step_slot(cudaStream_t stream, unsigned long long** tagged = nullptr) {
   const int dev = current_device();
+  const uintptr_t key_stream = reinterpret_cast<uintptr_t>(stream);
+  SlotHit& hit = tl_slot_hit;
+  if (hit.slot && hit.dev == dev && hit.stream == key_stream) {
+    if (tagged) *tagged = hit.tagged;
+    return hit.slot;
+  }
   std::lock_guard<std::mutex> lock(g_slot_mutex);
   unsigned* base = slot_base_for_device(dev);
   if (!base) return nullptr;
-  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(stream));
+  const auto key = std::make_pair(dev, key_stream);
   auto it = g_slot_of.find(key);
   int slot;
   if (it != g_slot_of.end()) {
@@ -819,8 +836,12 @@ unsigned* step_slot(cudaStream_t stream, unsigned long long** tagged = nullptr) 
     slot = g_slots_used[dev]++;
     g_slot_of[key] = slot;
   }
-  if (tagged) *tagged = g_tag_base[dev] + static_cast<size_t>(slot) * kStepTagWords;
-  return base + static_cast<size_t>(slot) * kStepSyncWords;
+  hit.dev = dev;
+  hit.stream = key_stream;
+  hit.slot = base + static_cast<size_t>(slot) * kStepSyncWords;
+  hit.tagged = g_tag_base[dev] + static_cast<size_t>(slot) * kStepTagWords;
+  if (tagged) *tagged = hit.tagged;
+  return hit.slot;
 }
 
 const void* step_kernel_ptr(int epl, int gh) {
@@ -972,10 +993,8 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   return true;
 }
 
-int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaStream_t stream) {
-  unsigned long long* tagged = nullptr;
-  unsigned* slot = step_slot(stream, &tagged);
-  if (!slot || !tagged) return fail(NVFP4DA_ERR_UNSUPPORTED, "no free synchronisation slot for another stream");
+int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaStream_t stream, unsigned* slot,
+             unsigned long long* tagged) {
   StepParams p{};
   p.x = a->x;
   p.g_in = a->input_norm_weight;
@@ -1240,21 +1259,28 @@ int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* 
     return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "unknown forward path %d", path);
   ForwardLayout L;
   if ((r = plan_forward(a, L))) return r;
-  // AUTO takes the one-kernel step where it applies: on B200 both paths take
-  // 22.1-22.2 us of device time on the canonical decode step, and the step
-  // needs one launch instead of three (host time of a direct call).
-  constexpr bool kAutoPrefersStep = true;
+  // AUTO takes the one-kernel step where it applies: on B200 it is faster
+  // than the three-kernel chain on the canonical decode step and needs one
+  // launch instead of three.  It needs a synchronisation slot for the
+  // stream; when every slot is taken AUTO takes the chain instead.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   StepPlan sp;
-  const bool step_ok = (path == NVFP4DA_PATH_STEP || (path == NVFP4DA_PATH_AUTO && kAutoPrefersStep)) &&
-                       plan_step(a, sp);
+  bool step_ok = (path == NVFP4DA_PATH_STEP || path == NVFP4DA_PATH_AUTO) && plan_step(a, sp);
   if (path == NVFP4DA_PATH_STEP && !step_ok)
     return fail(NVFP4DA_ERR_UNSUPPORTED, "the one-kernel decode step does not cover this configuration");
+  unsigned* slot = nullptr;
+  unsigned long long* tagged = nullptr;
+  if (step_ok && !(slot = step_slot(s, &tagged))) {
+    if (path == NVFP4DA_PATH_STEP)
+      return fail(NVFP4DA_ERR_UNSUPPORTED, "no free synchronisation slot for another stream (%d streams per device)",
+                  kStepSlots);
+    step_ok = false;
+  }
   const size_t need = step_ok ? std::max(L.total, sp.total) : L.total;
   if (!ws || ws_bytes < need)
     return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace too small (%zu < %zu bytes)", ws_bytes, need);
   if (!aligned(ws, 256)) return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace must be 256-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (step_ok) return run_step(a, sp, ws, s);
+  if (step_ok) return run_step(a, sp, ws, s, slot, tagged);
   char* base = static_cast<char*>(ws);
   const nvfp4da_forward_stages* st = a->stages;
   const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens, d = a->head_dim;

@@ -86,7 +86,7 @@ struct StepParams {
   size_t tag_words;             // the region's size, cleared when the epoch wraps
   unsigned* sync;    // slot
   unsigned long long timeout_ns;
-  // When the K/V tile and the O rows are requested (see the kernel).
+  // Diagnostic build only: when the K/V tile and the O rows are requested.
   int sched;
   // dynamic shared-memory layout (byte offsets); qs/qw/kv/q and comb overlay
   uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
@@ -326,13 +326,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   const unsigned long long deadline = global_ns() + p.timeout_ns;
 
   // ---- input slices of this CTA (none is written by the step): the QKV
-  // rows now, the K/V tile and the O rows later (p.sched), so that they do
-  // not queue ahead of the critical path.
-  // p.sched & 7: 0 K/V tile and O rows at launch; 1 both once the QKV rows
-  // have landed; 2 the K/V tile then, the O rows after the attention unit
-  // (at once where a CTA has none); 3 the K/V tile at launch, the O rows once
-  // the QKV rows have landed; 4 the K/V tile at launch, the O rows as in 2.
+  // rows now, the K/V tile and the O rows once the QKV rows have landed, so
+  // that they do not queue ahead of the critical path.  (The diagnostic
+  // build, -DNVFP4DA_PHASES, can request them at other times through
+  // p.sched & 7: 0 both at launch; 2 the K/V tile then, the O rows after the
+  // attention unit; 3 the K/V tile at launch, the O rows once the QKV rows
+  // have landed; 4 the K/V tile at launch, the O rows as in 2.)
+#ifdef NVFP4DA_PHASES
   const int sched = p.sched & 7;
+#else
+  constexpr int sched = 1;
+#endif
   const bool kv_at_launch = sched == 0 || sched == 3 || sched == 4;
   const int o_when = sched == 0 ? 0 : (sched == 2 || sched == 4 ? 2 : 1);
   auto issue_kv = [&]() {

@@ -3,16 +3,21 @@
 
 ``cuda_decoder_attention_forward_`` keeps the reference signature and its
 host-side validation (same exception types and messages, all raised before any
-launch), then runs one registered operator that issues three kernels chained
-by programmatic dependent launch: fused input RMSNorm + Q/K/V projection +
-per-head norm + RoPE + cache append; split-KV attention; O projection.  The
-trailing underscore means the physical ``[B, Hkv, C, D]`` caches are mutated in
-place at slots ``past_length .. past_length + T - 1``.
+launch), then runs one registered operator.  For a T = 1 decode step that it
+covers, the operator launches the one-kernel cooperative decode step (input
+RMSNorm, Q/K/V projection, per-head norm, RoPE, cache append, split-KV
+attention and O projection in one launch); otherwise three kernels chained by
+programmatic dependent launch (fused front half; split-KV attention -- the
+persistent streaming kernel for caches of 2,048 positions and more; O
+projection), or for prefill-sized inputs the modular chain on the tensor-core
+GEMM.  The trailing underscore means the physical ``[B, Hkv, C, D]`` caches are
+mutated in place at slots ``past_length .. past_length + T - 1``.
 """
 
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -21,6 +26,34 @@ from nvfp4_tensor import NVFP4Tensor, is_nvfp4_tensor
 
 _ops = torch.ops.cuda_nvfp4_decoder_attention
 _INT64_MAX = 2**63 - 1
+# Debug switch: NVFP4DA_CHECK_WAITS=1 makes every forward synchronise its
+# stream and raise if a bounded wait of the one-kernel step gave up.
+_CHECK_WAITS = os.environ.get("NVFP4DA_CHECK_WAITS", "") not in ("", "0")
+
+
+def check_wait_status(stream: torch.cuda.Stream | None = None) -> None:
+    """Raise ``RuntimeError`` if a bounded wait of a one-kernel decode step on
+    ``stream`` (default: the current stream) gave up since the last check.
+
+    The step kernel orders its phases by polling words in device memory, each
+    wait bounded in time; a wait that runs out records a flag and the kernel
+    finishes with garbage output instead of hanging.  The forward itself never
+    reads that flag back (it would cost a device-to-host synchronisation per
+    call); this function does, synchronises the stream and clears the flag.
+    """
+    import nvfp4da_capi
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    try:
+        flags = nvfp4da_capi.sync_status(s, clear=True)
+    except nvfp4da_capi.CapiError as e:
+        if e.status == nvfp4da_capi.ERR_UNSUPPORTED:  # no step slot: no one-kernel step ran on this stream
+            s.synchronize()
+            return
+        raise
+    if flags:
+        raise RuntimeError(f"a bounded wait of the one-kernel decode step timed out (flags 0x{flags:x}); "
+                           "the outputs of the forwards since the last check are not valid")
 
 
 def _tensor(name: str, value: object, rank: int) -> torch.Tensor:
@@ -151,9 +184,12 @@ def cuda_decoder_attention_forward_(x, input_norm_weight, q_weight, k_weight, v_
     if all(type(w) is NVFP4Tensor for w in ws4) and type(rms_eps) is float and type(rope_theta) in (float, int):
         (qp, qs, qg), (kp, ks, kg), (vp, vs, vg), (op, os_, og) = _flat(ws4)
         try:
-            return _ops.cuda_decoder_attention_forward_(x, input_norm_weight, qp, qs, qg, kp, ks, kg, vp, vs, vg,
-                                                        q_norm_weight, k_norm_weight, op, os_, og, k_cache, v_cache,
-                                                        past_length, rms_eps, float(rope_theta))
+            y = _ops.cuda_decoder_attention_forward_(x, input_norm_weight, qp, qs, qg, kp, ks, kg, vp, vs, vg,
+                                                     q_norm_weight, k_norm_weight, op, os_, og, k_cache, v_cache,
+                                                     past_length, rms_eps, float(rope_theta))
+            if _CHECK_WAITS:
+                check_wait_status()
+            return y
         except Exception:
             _validate(x, input_norm_weight, q_weight, k_weight, v_weight, q_norm_weight, k_norm_weight, out_weight,
                       k_cache, v_cache, past_length, rms_eps, rope_theta)
@@ -162,8 +198,11 @@ def cuda_decoder_attention_forward_(x, input_norm_weight, q_weight, k_weight, v_
         x, input_norm_weight, q_weight, k_weight, v_weight, q_norm_weight, k_norm_weight, out_weight, k_cache,
         v_cache, past_length, rms_eps, rope_theta)
     (qp, qs, qg), (kp, ks, kg), (vp, vs, vg), (op, os_, og) = _flat(ws)
-    return _ops.cuda_decoder_attention_forward_(x, g_in, qp, qs, qg, kp, ks, kg, vp, vs, vg, g_q, g_k, op, os_, og,
-                                                kc, vc, past_length, eps, theta)
+    y = _ops.cuda_decoder_attention_forward_(x, g_in, qp, qs, qg, kp, ks, kg, vp, vs, vg, g_q, g_k, op, os_, og,
+                                             kc, vc, past_length, eps, theta)
+    if _CHECK_WAITS:
+        check_wait_status()
+    return y
 
 
 def cuda_decoder_attention_forward_varlen_(x, input_norm_weight, q_weight, k_weight, v_weight, q_norm_weight,
@@ -187,8 +226,11 @@ def cuda_decoder_attention_forward_varlen_(x, input_norm_weight, q_weight, k_wei
         x, input_norm_weight, q_weight, k_weight, v_weight, q_norm_weight, k_norm_weight, out_weight, k_cache,
         v_cache, max_past_length, rms_eps, rope_theta)
     (qp, qs, qg), (kp, ks, kg), (vp, vs, vg), (op, os_, og) = _flat(ws)
-    return _ops.cuda_decoder_attention_forward_varlen_(x, g_in, qp, qs, qg, kp, ks, kg, vp, vs, vg, g_q, g_k, op,
-                                                       os_, og, kc, vc, past_lengths, max_past_length, eps, theta)
+    y = _ops.cuda_decoder_attention_forward_varlen_(x, g_in, qp, qs, qg, kp, ks, kg, vp, vs, vg, g_q, g_k, op,
+                                                    os_, og, kc, vc, past_lengths, max_past_length, eps, theta)
+    if _CHECK_WAITS:
+        check_wait_status()
+    return y
 
 
-__all__ = ["cuda_decoder_attention_forward_", "cuda_decoder_attention_forward_varlen_"]
+__all__ = ["cuda_decoder_attention_forward_", "cuda_decoder_attention_forward_varlen_", "check_wait_status"]

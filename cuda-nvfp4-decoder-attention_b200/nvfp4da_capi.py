@@ -1,7 +1,6 @@
 """ctypes binding of the C ABI (``include/nvfp4_decoder_attention.h``).
 
-This is the binding a non-PyTorch host would write; the
-parity tests and the benchmark call the kernels through it.  Tensors passed in
+This is the binding a non-PyTorch host would write; the parity tests and the benchmark call the kernels through it.  Tensors passed in
 must already live on the current CUDA device; the helpers only take their data
 pointers and sizes.  ``CapiError`` carries the library's status and message.
 """

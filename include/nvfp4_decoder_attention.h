@@ -151,9 +151,12 @@ typedef struct nvfp4da_forward_args {
 } nvfp4da_forward_args;
 
 /* Replaces the composed forward cuda_decoder_attention_forward_
- * (decoder_attention_cuda.py:149-417: 13 launches) with three kernels chained
- * by programmatic dependent launch: fused QKV (+ norms, RoPE, append), split-KV
- * attention, O projection.  Mutates the caches in place. */
+ * (decoder_attention_cuda.py:149-417: 13 launches).  A T = 1 decode step that
+ * the one-kernel step covers runs as one cooperative launch; other shapes run
+ * three kernels chained by programmatic dependent launch (fused QKV with the
+ * norms, RoPE and append; split-KV attention; O projection), or for
+ * B*T >= 128 the modular chain on the tensor-core GEMM.  Mutates the caches
+ * in place. */
 size_t nvfp4da_forward_workspace_size(const nvfp4da_forward_args* args);
 int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* workspace, size_t workspace_bytes,
                                       void* stream);
@@ -170,9 +173,10 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* wo
  * no stage outputs, and a K/V tile per split that fits in shared memory.  It
  * is a cooperative launch whose phases hand data to one another through a
  * library-owned region of the stream it is launched on (64 slots of 512 KB
- * per device; configurations whose hand-off words do not fit take the
- * chain): a graph that captured it must not be replayed concurrently with
- * other forwards issued to the capturing stream.  No counterpart in the reference
+ * per device, one per stream, never released; configurations whose hand-off
+ * words do not fit, and streams beyond the 64th, take the chain under AUTO):
+ * a graph that captured it must not be replayed concurrently with other
+ * forwards issued to the capturing stream.  No counterpart in the reference
  * (its forward is always the modular chain). */
 #define NVFP4DA_PATH_AUTO 0
 #define NVFP4DA_PATH_CHAIN 1

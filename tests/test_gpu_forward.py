@@ -215,3 +215,50 @@ def test_non_default_stream_orders_every_stage():
         result = out.to("cpu", non_blocking=True)
     side.synchronize()
     assert torch.equal(result.view(torch.int16), expected.cpu().view(torch.int16))
+
+
+def test_config2_batched_decode_full_size_sampled():
+    """configs[2] at full size: B=64, T=1, P_b ~ U[1024, 8191] (seeded), C=8192,
+    device-side per-sequence lengths.  Stage-isolated parity on sampled
+    sequences (the oracle applied to the GPU's own upstream rows; the context
+    over each sampled sequence's P_b + 1 keys), and every sequence's cache
+    prefix and suffix bit for bit unchanged."""
+    import synthetic
+
+    shape = synthetic.batched_shape()
+    b, h, hkv, d = shape.batch, shape.hidden, shape.kv_heads, shape.head_dim
+    hq = h // d
+    pasts = np.array(shape.past_lengths, dtype=np.int64)
+    inp = synthetic.make_decode_inputs(shape, seed=2, cache_device="cuda")
+    host_w = {k: oracle.quantize(w.numpy()) for k, w in inp.weights_fp32.items()}
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    kc, vc = inp.k_cache, inp.v_cache
+    kc_before, vc_before = kc.clone(), vc.clone()
+    pl = torch.from_numpy(pasts).cuda()
+    out, st = run_forward(inp.x.cuda(), inp.input_norm_weight.cuda(), ws, inp.q_norm_weight.cuda(),
+                          inp.k_norm_weight.cuda(), kc, vc, 0, past_lengths=pl, max_past=int(pasts.max()))
+    for i in range(b):  # only slot P_b of each sequence changes
+        p = int(pasts[i])
+        assert torch.equal(kc[i, :, :p].view(torch.int16), kc_before[i, :, :p].view(torch.int16))
+        assert torch.equal(kc[i, :, p + 1:].view(torch.int16), kc_before[i, :, p + 1:].view(torch.int16))
+        assert torch.equal(vc[i, :, :p].view(torch.int16), vc_before[i, :, :p].view(torch.int16))
+        assert torch.equal(vc[i, :, p + 1:].view(torch.int16), vc_before[i, :, p + 1:].view(torch.int16))
+    out_bits = host_bits(out)
+    x, g_in = host_bits(inp.x), host_bits(inp.input_norm_weight)
+    g_q, g_k = host_bits(inp.q_norm_weight), host_bits(inp.k_norm_weight)
+    for i in sorted({0, int(np.argmin(pasts)), int(np.argmax(pasts)), 17, 40, b - 1}):
+        p = int(pasts[i])
+        r = slice(i, i + 1)
+        xn = st["input_normalized"][r]
+        assert_bitwise(xn, oracle.rms_norm(x[r], g_in, 1e-6))
+        for key, stage in (("q", "q_projected"), ("k", "k_projected"), ("v", "v_projected")):
+            assert_stage_policy(st[stage][r], oracle.w4a16_linear(xn, host_w[key]))
+        qn, kn = st["q_normalized"][r], st["k_normalized"][r]
+        assert_bitwise(qn, oracle.rms_norm(st["q_projected"][r].reshape(1, 1, hq, d), g_q, 1e-6))
+        assert_bitwise(kn, oracle.rms_norm(st["k_projected"][r].reshape(1, 1, hkv, d), g_k, 1e-6))
+        assert_bitwise(st["q_rope"][r], oracle.apply_rope(qn, p, 1e4))
+        k_seq, v_seq = host_bits(kc[r, :, :p + 1]), host_bits(vc[r, :, :p + 1])
+        assert_bitwise(k_seq[0, :, p], oracle.apply_rope(kn, p, 1e4)[0, 0])
+        assert_bitwise(v_seq[0, :, p], st["v_projected"][r].reshape(hkv, d))
+        assert_attention_policy(st["context"][r], oracle.gqa_attention(st["q_rope"][r], k_seq, v_seq, p))
+        assert_stage_policy(out_bits[r], oracle.w4a16_linear(st["context"][r].reshape(1, 1, hq * d), host_w["o"]))

@@ -7,9 +7,12 @@ cooperative launch.  Per case:
 * the cache: every slot but P_b unchanged bit for bit; the appended V row
   within one BF16 step of the oracle's V projection, the appended K row within
   the attention policy of the oracle's K after norm and RoPE;
+* the appended K and V rows bit for bit equal to the chain's on the same
+  inputs (the step recomputes the projections, the per-head norm and RoPE in
+  its own code, so this pins them to the chain's bit-exact stages);
 * no bounded wait gave up (the stream's sync status stays 0).
-Plus repeated launches, graph replay, two streams at once, and the bounded-
-wait self-test.
+Plus repeated launches, graph replay, two streams at once, more streams than
+the step has synchronisation slots, and the bounded-wait self-test.
 """
 
 from __future__ import annotations
@@ -81,6 +84,9 @@ def test_step_matches_oracle_and_chain(b, h, hkv, d, pasts, c):
     assert fw.step_supported
     fw.run(path=nvfp4da_capi.PATH_STEP)
     assert nvfp4da_capi.sync_status() == 0
+    import decoder_attention_cuda
+
+    decoder_attention_cuda.check_wait_status()  # the drop-in module's check: no wait gave up
     out_bits, kc_bits, vc_bits = host_bits(out), host_bits(kc), host_bits(vc)
 
     kc2, vc2 = inp.k_cache.cuda(), inp.v_cache.cuda()
@@ -88,6 +94,9 @@ def test_step_matches_oracle_and_chain(b, h, hkv, d, pasts, c):
     fw2.run(path=nvfp4da_capi.PATH_CHAIN)
     torch.cuda.synchronize()
     chain_bits = host_bits(out2)
+    # The appended rows (and so the whole caches) equal the chain's bit for bit.
+    np.testing.assert_array_equal(kc_bits, host_bits(kc2))
+    np.testing.assert_array_equal(vc_bits, host_bits(vc2))
 
     g_q, g_k = host_bits(inp.q_norm_weight), host_bits(inp.k_norm_weight)
     ref = oracle.decoder_attention_nvfp4(host_bits(inp.x), host_bits(inp.input_norm_weight), host_w["q"],
@@ -158,6 +167,65 @@ def test_step_on_two_streams_at_once():
     for (_, out), st in zip(runs, streams):
         assert torch.equal(out.view(torch.int16), expected.view(torch.int16))
         assert nvfp4da_capi.sync_status(st) == 0
+
+
+def test_more_streams_than_synchronisation_slots():
+    """The step keeps per-stream hand-off slots (64 per device, never
+    released).  Past them, AUTO takes the chain instead of failing: 70 fresh
+    streams all give the step's or the chain's bits.  Runs in a child process:
+    the slots it uses up stay used for the life of the process."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent
+    code = (f"import sys; sys.path[:0] = [{str(here)!r}, {str(here.parent)!r}, "
+            f"{str(here.parent / 'cuda-nvfp4-decoder-attention_b200')!r}]\n"
+            "import test_gpu_step as t; t._many_streams_child()\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "many-streams ok" in r.stdout
+
+
+def _many_streams_child():
+    import nvfp4da_capi
+
+    inp, host_w = make_case(1, 3072, 6, 128, 511, 1024, seed=8)
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    expect = {}
+    for path in (nvfp4da_capi.PATH_STEP, nvfp4da_capi.PATH_CHAIN):
+        fw, out = forward(inp, ws, 511, inp.k_cache.cuda(), inp.v_cache.cuda(), path)
+        fw.run(path=path)
+        torch.cuda.synchronize()
+        expect[path] = out.view(torch.int16).clone()
+    fw, out = forward(inp, ws, 511, inp.k_cache.cuda(), inp.v_cache.cuda(), nvfp4da_capi.PATH_AUTO)
+    # Fresh CUDA streams (torch.cuda.Stream() cycles through a fixed pool).
+    from cuda.bindings import runtime as cudart
+
+    streams = []
+    for _ in range(70):
+        err, handle = cudart.cudaStreamCreate()
+        assert int(err) == 0
+        streams.append(torch.cuda.ExternalStream(int(handle)))
+    took = {nvfp4da_capi.PATH_STEP: 0, nvfp4da_capi.PATH_CHAIN: 0}
+    for st in streams:
+        out.zero_()
+        torch.cuda.synchronize()
+        fw.run(st)
+        st.synchronize()
+        got = out.view(torch.int16)
+        match = [p for p, e in expect.items() if torch.equal(got, e)]
+        assert match, "output of neither path"
+        took[match[0]] += 1
+    if not torch.equal(expect[nvfp4da_capi.PATH_STEP], expect[nvfp4da_capi.PATH_CHAIN]):
+        assert took[nvfp4da_capi.PATH_CHAIN] >= 70 - 64
+    with pytest.raises(nvfp4da_capi.CapiError) as e:  # an explicit step request still reports the limit
+        fw.run(streams[-1], path=nvfp4da_capi.PATH_STEP)
+    assert e.value.status == nvfp4da_capi.ERR_UNSUPPORTED
+    torch.cuda.synchronize()
+    for st in streams:
+        cudart.cudaStreamDestroy(st.cuda_stream)
+    print("many-streams ok", flush=True)
 
 
 def test_auto_path_matches_one_of_the_explicit_paths():

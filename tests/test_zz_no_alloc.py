@@ -5,10 +5,13 @@ budget or a host whose allocator owns all device memory), the library offers
 nvfp4da_decoder_attention_forward_noalloc: the same forward, with its scratch
 taken from an 8 MiB array built into the library instead of a caller workspace.
 These tests call it through the C ABI and check it against the workspace entry
-point on two calls in a row, for the canonical decode step and for a long
-single-sequence step whose attention combines its splits through the scratch
-counters (which must be cleared between calls).  This file is named so pytest
-collects it last.
+point on two calls in a row: the canonical decode step (the one-kernel step,
+which keeps nothing in the scratch), and two steps that take the kernel chain
+and so keep their q, context, split partials and combine counters in the
+array -- a batch of 9 long sequences (the streaming attention kernel) and a
+two-token step (global split partials of the short-cache kernel).  The
+counters must start each call at zero although the array keeps the last
+call's contents.  This file is named so pytest collects it last.
 """
 
 from __future__ import annotations
@@ -51,13 +54,15 @@ def forward_pair(inp, ws, p):
     return out
 
 
-@pytest.mark.parametrize("b,t,h,hkv,d,p,c", [
-    (1, 1, 3072, 6, 128, 511, 1024),  # configs[0]: split combine inside thread-block clusters
-    (1, 1, 512, 1, 128, 4000, 4096),  # one sequence, many splits: combine through scratch counters
+@pytest.mark.parametrize("b,t,h,hkv,d,p,c,step", [
+    (1, 1, 3072, 6, 128, 511, 1024, True),    # configs[0]: the one-kernel step
+    (9, 1, 768, 2, 128, 3000, 3072, False),   # B > 8: chain, streaming attention, counters in the array
+    (1, 2, 3072, 6, 128, 1500, 2048, False),  # T = 2: chain, 47 splits combined through the array
 ])
-def test_noalloc_forward_matches_workspace_forward_twice(b, t, h, hkv, d, p, c):
+def test_noalloc_forward_matches_workspace_forward_twice(b, t, h, hkv, d, p, c, step):
     inp, ws = make_case(b, t, h, hkv, d, p, c, seed=101)
     (ref_fw, ref_y, ref_kc, ref_vc), (na_fw, na_y, na_kc, na_vc) = forward_pair(inp, ws, p)
+    assert na_fw.step_supported == step
     for call in range(2):  # the second call reuses the array left by the first
         ref_fw.run()
         na_fw.run_noalloc()
