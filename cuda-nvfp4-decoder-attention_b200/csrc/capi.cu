@@ -870,6 +870,8 @@ struct StepPlan {
   int splits, split_len, grid;
   uint32_t smem;
   uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
+  int o_predecode, od_ld;
+  uint32_t off_od;
   size_t proj, ctx, part_o, part_ml, total;  // workspace offsets / bytes
 };
 
@@ -962,16 +964,30 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   // split weights of the combine) and q.
   const uint64_t tile = 2ull * split_len * d * 2, smo = 1ull * kStepWarps * group * d * 4,
                  comb_w = 2ull * group * splits * 4;
-  s.off_qs = take(rq * ks);
-  s.off_qw = take(rq * kb);
-  s.off_kv = take(std::max(tile, std::max(smo, comb_w)));
-  s.off_q = take(group * d * 4);
   const uint64_t items = nb * hq;
   s.off_os = take(rows_big * ks);
   s.off_ow = take(rows_big * kb);
   s.off_xs = take(nb * k * 2);
   s.off_x16 = take(nb * k * 2);
   s.off_red = take(kMmaWarps * 128 * 4);
+  // Early-phase buffers: QKV rows, the K/V tile (later the warps' o vectors,
+  // then the split weights of the combine) and q.  The O rows decoded ahead
+  // overlay them once they are consumed.
+  s.off_qs = take(rq * ks);
+  s.off_qw = take(rq * kb);
+  s.off_kv = take(std::max(tile, std::max(smo, comb_w)));
+  s.off_q = take(group * d * 4);
+  const uint64_t early = off - s.off_qs;
+  s.od_ld = static_cast<int>(k + 8);  // f16 row stride: 16 bytes of padding keep ldmatrix conflict-free
+  const uint64_t od_bytes = static_cast<uint64_t>(rows_big) * s.od_ld * 2;
+  s.off_od = s.off_qs;
+  s.o_predecode = 0;
+  if (od_bytes <= early) {
+    s.o_predecode = 1;
+  } else if (off + (od_bytes - early) + static_smem(fn) <= kMaxDynSmem) {
+    take(od_bytes - early);
+    s.o_predecode = 1;
+  }
   if (off + static_smem(fn) > kMaxDynSmem) return false;
   // The MMA tiles read up to o_tile_rows rows; the rows past the CTA's own
   // land in the buffers that follow (in bounds, their outputs discarded).
@@ -1049,6 +1065,9 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   p.off_xs = pl.off_xs;
   p.off_x16 = pl.off_x16;
   p.off_red = pl.off_red;
+  p.o_predecode = pl.o_predecode;
+  p.off_od = pl.off_od;
+  p.od_ld = pl.od_ld;
   // RoPE cos/sin at position past_length, the host arithmetic of qkv_params.
   p.rope_host_ok = 0;
   if (!a->past_lengths) {

@@ -45,6 +45,7 @@
 #pragma once
 
 #include "attention.cuh"
+#include "attention_prefill.cuh"  // ldsm_x4
 #include "elementwise.cuh"
 #include "gemv_mma.cuh"
 #include "qkv_fused.cuh"  // kMaxHeadDim
@@ -90,6 +91,11 @@ struct StepParams {
   int sched;
   // dynamic shared-memory layout (byte offsets); qs/qw/kv/q and comb overlay
   uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
+  // O rows decoded ahead into f16 rows at off_od (stride od_ld halves), which
+  // overlays the QKV rows, the K/V tile and q once they are consumed.
+  int o_predecode;
+  uint32_t off_od;
+  int od_ld;
   // cos/sin of RoPE at position past_length (rope_host_ok), else computed on the device
   int rope_host_ok;
   float2 rope_host[kMaxHeadDim / 2];
@@ -208,6 +214,76 @@ __device__ __forceinline__ void poll_tagged(const unsigned long long* const (&sr
   }
 }
 
+// ---------------------------------------------------------------- O rows decoded ahead
+// Decode `rows` weight rows (packed [rows][K/2], scales [rows][K/16], both in
+// shared memory) into f16 rows of stride `ld` halves: (q * beta) exactly, in
+// natural k order.  Called by every thread; the caller synchronises.
+__device__ __forceinline__ void predecode_rows_f16(const uint8_t* w_smem, const uint8_t* s_smem, int64_t k, int rows,
+                                                   __half* dst, int ld) {
+  const int chunks = static_cast<int>(k / 32);  // 16 packed bytes = 32 k = two scale blocks
+  const int64_t kb = k / 2, ks = k / 16;
+  for (int i = threadIdx.x; i < rows * chunks; i += blockDim.x) {
+    const int r = i / chunks, c = i % chunks;
+    const uint4 w = *reinterpret_cast<const uint4*>(w_smem + r * kb + 16 * c);
+    const uint32_t s2 = *reinterpret_cast<const uint16_t*>(s_smem + r * ks + 2 * c);
+    const uint32_t sc[2] = {ue4m3_to_f16x2_dup(s2), ue4m3_to_f16x2_dup(s2 >> 8)};
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    uint4* o = reinterpret_cast<uint4*>(dst + static_cast<int64_t>(r) * ld + 32 * c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // word q: k = 32 c + 8 q .. + 7 (block 2 c + q / 2)
+      uint32_t h[4];
+      e2m1x8_to_f16x2x4(wv[q], h);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = hmul2_u32(h[j], sc[q >> 1]);
+      o[q] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+  }
+}
+
+// The O pass over rows decoded ahead: A fragments by ldmatrix from the f16
+// rows (stride `ld` halves), B from the activation operand rows (f16, or
+// bf16 with A converted -- exact either way), 16 k per MMA, four accumulator
+// chains; then the cross-warp reduction into out[r * 8 + n].  `rows` is
+// tile-padded; rows at or past `valid_rows` are never read (a tile's upper
+// half past them re-reads its lower half) and their outputs are discarded.
+template <bool F16>
+__device__ __forceinline__ void mma_pass_decoded(const __half* a_smem, int ld, const uint16_t* xop, int64_t k,
+                                                 int rows, int valid_rows, int mgv, float* red, float* out) {
+  const WarpSlice ws = warp_slice(rows, k);
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float d[4][4] = {};
+  if (ws.tile * 16 < valid_rows) {
+    const bool hi = ws.tile * 16 + 8 < valid_rows;
+    const int mat = lane >> 3;
+    const int row = ws.tile * 16 + (lane & 7) + ((mat & 1) && hi ? 8 : 0);
+    const uint32_t abase = smem_u32(a_smem) + static_cast<uint32_t>((row * ld + (mat >> 1) * 8) * 2);
+    const bool has_n = g < mgv;
+    const uint16_t* xrow = xop + static_cast<int64_t>(has_n ? g : 0) * k + 2 * t;
+#pragma unroll 1
+    for (int s = ws.s0; s < ws.s1; ++s) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int k0 = s * kStepK + 16 * j;
+        uint32_t a[4];
+        ldsm_x4(abase + k0 * 2, a[0], a[1], a[2], a[3]);
+        const uint32_t b0 = has_n ? *reinterpret_cast<const uint32_t*>(xrow + k0) : 0u;
+        const uint32_t b1 = has_n ? *reinterpret_cast<const uint32_t*>(xrow + k0 + 8) : 0u;
+        if constexpr (F16) {
+          mma_f16(d[j & 3], a, b0, b1);
+        } else {
+          const uint32_t ab[4] = {f16x2_to_bf16x2(a[0]), f16x2_to_bf16x2(a[1]), f16x2_to_bf16x2(a[2]),
+                                  f16x2_to_bf16x2(a[3])};
+          mma_bf16(d[j & 3], ab, b0, b1);
+        }
+      }
+    }
+  }
+  float dsum[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dsum[i] = (d[0][i] + d[1][i]) + (d[2][i] + d[3][i]);
+  reduce_tiles(dsum, rows, red, out);
+}
+
 // ---------------------------------------------------------------- the kernel
 template <int EPL, int GH>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
@@ -258,14 +334,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   const bool has_qkv = cta < p.n_qkv_blocks;
   const int n_units = static_cast<int>(nb * hkv) * ns;
   const bool has_attn = cta < n_units;
+  // O rows: the o_n_big CTAs at the end of the grid take o_rows_big rows,
+  // the others o_rows_small (the attention units sit at the start).
   int64_t orow0;
   int o_rows;
-  if (cta < p.o_n_big) {
-    o_rows = p.o_rows_big;
-    orow0 = static_cast<int64_t>(cta) * p.o_rows_big;
-  } else {
+  const int o_n_small = static_cast<int>(gridDim.x) - p.o_n_big;
+  if (cta < o_n_small) {
     o_rows = p.o_rows_small;
-    orow0 = static_cast<int64_t>(p.o_n_big) * p.o_rows_big + static_cast<int64_t>(cta - p.o_n_big) * p.o_rows_small;
+    orow0 = static_cast<int64_t>(cta) * p.o_rows_small;
+  } else {
+    o_rows = p.o_rows_big;
+    orow0 = static_cast<int64_t>(o_n_small) * p.o_rows_small + static_cast<int64_t>(cta - o_n_small) * p.o_rows_big;
   }
   const int o_valid = orow0 < k ? static_cast<int>((k - orow0) < o_rows ? (k - orow0) : o_rows) : 0;
   const bool has_o = o_valid > 0;
@@ -708,6 +787,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   // ---- O projection
   if (has_o) {
+    // Decode the O rows into f16 while the context is still being computed
+    // (every thread; the weight decode leaves the critical path).
+    __half* od = reinterpret_cast<__half*>(smem + p.off_od);
+    if (p.o_predecode) {
+      // The decoded rows overlay the K/V tile region, which the attention
+      // unit's combine may still be reading in other warps.
+      if (has_attn) __syncthreads();
+      mbar_spin_until(&bar_o, 0, deadline, err);
+      predecode_rows_f16(ow_smem, os_smem, k, o_valid, od, p.od_ld);
+      NVFP4DA_PHASE(19);
+    }
     // The context, as the splits publish it, into the BF16 operand rows.
     bool o_f16;
     {
@@ -767,13 +857,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     }
     NVFP4DA_PHASE(10);
     const bool f16 = o_f16;
-    mbar_spin_until(&bar_o, 0, deadline, err);
-    NVFP4DA_PHASE(11);
-    if (f16)
-      mma_gemv_pass_smem<true, 4>(ow_smem, os_smem, reinterpret_cast<const uint16_t*>(x16), k, p.o_tile_rows,
-                                  o_valid, mrows, mred, outv);
-    else
-      mma_gemv_pass_smem<false, 4>(ow_smem, os_smem, x_stage, k, p.o_tile_rows, o_valid, mrows, mred, outv);
+    if (p.o_predecode) {
+      NVFP4DA_PHASE(11);
+      if (f16)
+        mma_pass_decoded<true>(od, p.od_ld, reinterpret_cast<const uint16_t*>(x16), k, p.o_tile_rows, o_valid, mrows,
+                               mred, outv);
+      else
+        mma_pass_decoded<false>(od, p.od_ld, x_stage, k, p.o_tile_rows, o_valid, mrows, mred, outv);
+    } else {
+      mbar_spin_until(&bar_o, 0, deadline, err);
+      NVFP4DA_PHASE(11);
+      if (f16)
+        mma_gemv_pass_smem<true, 4>(ow_smem, os_smem, reinterpret_cast<const uint16_t*>(x16), k, p.o_tile_rows,
+                                    o_valid, mrows, mred, outv);
+      else
+        mma_gemv_pass_smem<false, 4>(ow_smem, os_smem, x_stage, k, p.o_tile_rows, o_valid, mrows, mred, outv);
+    }
     const float gamma = gamma_o;
     for (int i = threadIdx.x; i < o_valid * mrows; i += kStepThreads) {
       const int n = i / o_valid, r = i % o_valid;
