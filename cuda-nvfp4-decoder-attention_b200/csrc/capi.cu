@@ -700,6 +700,13 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   return NVFP4DA_OK;
 }
 
+// theta^(2m/D) rounded to FP32 with the arithmetic of reference
+// decoder_attention.py:237-257 (FP32 exponent, the power in double rounded once).
+float rope_denominator(const nvfp4da_forward_args* a, int64_t m) {
+  const float expo = static_cast<float>(2 * m) / static_cast<float>(a->head_dim);
+  return static_cast<float>(std::pow(static_cast<double>(a->rope_theta), static_cast<double>(expo)));
+}
+
 QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
   QkvParams p{};
   p.x = a->x;
@@ -740,6 +747,7 @@ QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
   // exponent 2m/D, FP32 theta^exponent, FP32 angle = p / denominator, FP32
   // cos / sin -- each transcendental evaluated in double and rounded once.
   p.rope_rows = 0;
+  for (int64_t m = 0; m < a->head_dim / 2 && m < kMaxHeadDim / 2; ++m) p.rope_denom[m] = rope_denominator(a, m);
   if (!a->past_lengths && a->tokens <= kMaxRopeRows && a->head_dim <= kMaxHeadDim) {
     const int64_t d = a->head_dim;
     for (int64_t t = 0; t < a->tokens; ++t) {
@@ -1069,7 +1077,8 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   p.off_od = pl.off_od;
   p.od_ld = pl.od_ld;
   // RoPE cos/sin at position past_length, the host arithmetic of qkv_params.
-  p.rope_host_ok = 0;
+  p.rope_host_ok = 2;
+  for (int64_t m = 0; m < a->head_dim / 2; ++m) p.rope_host[m] = make_float2(rope_denominator(a, m), 0.0f);
   if (!a->past_lengths) {
     const int64_t d = a->head_dim, pos = a->past_length;
     for (int64_t m = 0; m < d / 2; ++m) {

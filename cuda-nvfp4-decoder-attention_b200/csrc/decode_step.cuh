@@ -96,7 +96,9 @@ struct StepParams {
   int o_predecode;
   uint32_t off_od;
   int od_ld;
-  // cos/sin of RoPE at position past_length (rope_host_ok), else computed on the device
+  // RoPE: rope_host_ok == 1: (cos, sin) at position past_length; == 2: .x holds
+  // theta^(2m/D) in FP32 and the angle and its cos / sin come from the device
+  // (per-sequence lengths read on the device).
   int rope_host_ok;
   float2 rope_host[kMaxHeadDim / 2];
 };
@@ -453,7 +455,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   // ---- input RMSNorm of the activation rows -> MMA operand, QKV GEMV
   if (has_qkv) {
-    bool f16 = prep_rows_regs<NCH, true>(p.x, k, mrows, gch, p.eps, x_stage, x16, escale, redf, redd, nullptr);
+    bool f16 = mrows > 1 ? prep_rows_warp<true>(p.x, p.g_in, k, mrows, p.eps, x_stage, x16, escale, nullptr)
+                         : prep_rows_regs<NCH, true>(p.x, k, mrows, gch, p.eps, x_stage, x16, escale, redf, redd, nullptr);
     NVFP4DA_PHASE(2);
     mbar_spin_until(&bar_qkv, 0, deadline, err);
     if (threadIdx.x == 0) {
@@ -538,11 +541,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         uint16_t r0 = n0, r1 = n1;
         if (pb != 0) {
           float c, sn;
-          if (p.rope_host_ok) {
+          if (p.rope_host_ok == 1) {
             c = p.rope_host[pr].x;
             sn = p.rope_host[pr].y;
           } else {
-            rope_cos_sin(pb, pr, d, p.theta, c, sn);
+            rope_cos_sin_denom(pb, p.rope_host[pr].x, c, sn);
           }
           rope_pair(bf16_bits_to_f32(n0), bf16_bits_to_f32(n1), c, sn, r0, r1);
         }

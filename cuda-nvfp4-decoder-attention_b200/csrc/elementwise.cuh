@@ -61,6 +61,16 @@ __device__ __forceinline__ void rope_cos_sin(int64_t pos, int64_t pair, int64_t 
   s = static_cast<float>(sd);
 }
 
+// The same with theta^(2m/D) rounded to FP32 given (computed on the host with
+// the arithmetic above): only the angle and its cos / sin on the device.
+__device__ __forceinline__ void rope_cos_sin_denom(int64_t pos, float denom, float& c, float& s) {
+  const float angle = __fdiv_rn(static_cast<float>(pos), denom);
+  double sd, cd;
+  sincos(static_cast<double>(angle), &sd, &cd);
+  c = static_cast<float>(cd);
+  s = static_cast<float>(sd);
+}
+
 __device__ __forceinline__ void rope_pair(float xe, float xo, float c, float s, uint16_t& ye, uint16_t& yo) {
   ye = f32_to_bf16_bits(__fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, s)));
   yo = f32_to_bf16_bits(__fadd_rn(__fmul_rn(xe, s), __fmul_rn(xo, c)));

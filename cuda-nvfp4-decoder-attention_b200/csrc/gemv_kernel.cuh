@@ -141,7 +141,9 @@ __global__ void __launch_bounds__(kMmaThreads, 2) mma_gemv_kernel(GemvParams p) 
     constexpr int NCH = 2;  // register path for K <= 4096
     if ((k / 8) <= NCH * kMmaThreads && aligned16(p.x)) {
       const uint4 none[NCH] = {};
-      f16 = prep_rows_regs<NCH, false>(p.x + m0 * k, k, mgv, none, 0.0f, x_stage, x16, escale, redf, redd, nullptr);
+      f16 = mgv > 1 ? prep_rows_warp<false>(p.x + m0 * k, nullptr, k, mgv, 0.0f, x_stage, x16, escale, nullptr)
+                    : prep_rows_regs<NCH, false>(p.x + m0 * k, k, mgv, none, 0.0f, x_stage, x16, escale, redf, redd,
+                                                 nullptr);
     } else {
       load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
       __syncthreads();

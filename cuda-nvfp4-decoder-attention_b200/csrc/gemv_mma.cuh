@@ -505,4 +505,91 @@ __device__ __forceinline__ bool prep_rows_regs(const uint16_t* x, int64_t k, int
   return __syncthreads_or(inexact) == 0;
 }
 
+// Several activation rows at once (mgv >= 2): warp w prepares row w (and
+// w + 8, ...) alone, in place in its x_stage row -- the same per-row
+// arithmetic as prep_rows_regs (optional RMSNorm with the FP64 sum of squares,
+// exact in any order, then the power-of-two f16 operand) with warp reductions
+// only, so the rows proceed in parallel and the CTA meets one barrier in all.
+// Each lane only rereads the 16-byte chunks it wrote itself.  `g` is the norm
+// gain in global memory (read through L1; every warp reads the same chunks).
+// Same outputs as prep_rows_regs.
+template <bool NORM, bool L2_ONLY = false>
+__device__ __forceinline__ bool prep_rows_warp(const uint16_t* x, const uint16_t* g, int64_t k, int mgv, float eps,
+                                               uint16_t* x_stage, __half* x16, float* escale, uint16_t* dbg) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int kv8 = static_cast<int>(k / 8);
+  int inexact = 0;
+  for (int m = warp; m < mgv; m += kMmaWarps) {
+    uint4* row = reinterpret_cast<uint4*>(x_stage + m * k);  // this warp's row, staged in shared memory
+    const uint4* src = reinterpret_cast<const uint4*>(x + m * k);
+    double ss = 0.0;
+    for (int idx = lane; idx < kv8; idx += 32) {
+      const uint4 v = L2_ONLY ? __ldcg(src + idx) : src[idx];
+      row[idx] = v;
+      if constexpr (NORM) {
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float a = __uint_as_float(wv[q] << 16), b = __uint_as_float(wv[q] & 0xffff0000u);
+          ss += static_cast<double>(a * a) + static_cast<double>(b * b);
+        }
+      }
+    }
+    float mx = 0.0f;
+    if constexpr (NORM) {
+      ss = warp_sum_f64(ss);  // also orders the row's shared-memory writes before the reads below
+      const float inv = rms_inverse(static_cast<float>(ss), static_cast<float>(k), eps);
+      for (int idx = lane; idx < kv8; idx += 32) {
+        const uint4 v = row[idx], gg = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w}, wg[4] = {gg.x, gg.y, gg.z, gg.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float lo = __fmul_rn(__fmul_rn(__uint_as_float(wv[q] << 16), inv), __uint_as_float(wg[q] << 16));
+          const float hi =
+              __fmul_rn(__fmul_rn(__uint_as_float(wv[q] & 0xffff0000u), inv), __uint_as_float(wg[q] & 0xffff0000u));
+          o[q] = static_cast<uint32_t>(f32_to_bf16_bits(lo)) | (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+          mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(o[q] << 16)), fabsf(__uint_as_float(o[q] & 0xffff0000u))));
+        }
+        const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
+        row[idx] = nv;
+        if (dbg) reinterpret_cast<uint4*>(dbg + m * k)[idx] = nv;
+      }
+    } else {
+      for (int idx = lane; idx < kv8; idx += 32) {
+        const uint4 v = row[idx];
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(wv[q] << 16)), fabsf(__uint_as_float(wv[q] & 0xffff0000u))));
+        if (dbg) reinterpret_cast<uint4*>(dbg + m * k)[idx] = v;
+      }
+    }
+    mx = warp_max_f32(mx);  // each lane reads back only what it wrote, so no other ordering is needed
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+      const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 127;  // floor(log2) for normals
+      e = 14 - (ex < -126 ? -126 : ex);
+      e = e > 126 ? 126 : (e < -126 ? -126 : e);
+    }
+    const float sc = __uint_as_float(static_cast<uint32_t>(127 + e) << 23);   // 2^e
+    const float isc = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e
+    if (lane == 0) escale[m] = isc;
+    for (int idx = lane; idx < kv8; idx += 32) {
+      const uint4 v = row[idx];
+      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float a = __uint_as_float(wv[q] << 16), b = __uint_as_float(wv[q] & 0xffff0000u);
+        const __half2 h = __floats2half2_rn(a * sc, b * sc);
+        inexact |= (__low2float(h) * isc != a) | (__high2float(h) * isc != b);  // round trip gives x back
+        o[q] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      reinterpret_cast<uint4*>(x16 + m * k)[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  return __syncthreads_or(inexact) == 0;
+}
+
 }  // namespace nvfp4da

@@ -63,6 +63,8 @@ struct QkvParams {
   // positions are the scalar past_length + t (rope_rows == 0: on the device).
   int rope_rows;
   float2 rope_host[kMaxRopeRows][kMaxHeadDim / 2];
+  // theta^(2m/D) rounded to FP32, from the host, for positions read on the device.
+  float rope_denom[kMaxHeadDim / 2];
 };
 
 // Dynamic shared memory of the fused kernel: the MMA-GEMV layout followed by
@@ -179,7 +181,7 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
         c = cs.x;
         sn = cs.y;
       } else if (pos != 0) {
-        rope_cos_sin(pos, pr, d, p.theta, c, sn);
+        rope_cos_sin_denom(pos, p.rope_denom[pr], c, sn);
       }
       rope_cs[m][pr] = make_float2(c, sn);
     }
@@ -226,7 +228,9 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
         gains_ready = true;
       }
       NVFP4DA_PHASE(4);
-      f16 = prep_rows_regs<NCH, true>(p.x + m0 * k, k, mgv, gch, p.eps, x_stage, x16, escale, redf, redd,
+      f16 = mgv > 1 ? prep_rows_warp<true>(p.x + m0 * k, p.g_in, k, mgv, p.eps, x_stage, x16, escale,
+                                           (p.dbg_xnorm && blockIdx.x == 0) ? p.dbg_xnorm + m0 * k : nullptr)
+                    : prep_rows_regs<NCH, true>(p.x + m0 * k, k, mgv, gch, p.eps, x_stage, x16, escale, redf, redd,
                                       (p.dbg_xnorm && blockIdx.x == 0) ? p.dbg_xnorm + m0 * k : nullptr);
     } else {
       load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
