@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) mma_gemv_kernel(GemvParams p) 
   uint8_t* s_smem = smem + L.s_off();
   uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + L.xs_off());
   __half* x16 = reinterpret_cast<__half*>(smem + L.x16_off());
+  const bool aliased = reinterpret_cast<const void*>(x16) == reinterpret_cast<const void*>(x_stage);
   float* red = reinterpret_cast<float*>(smem + L.red_off());
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * ROWS;
   const int valid_rows = static_cast<int>((p.n - row0) < ROWS ? (p.n - row0) : ROWS);
@@ -141,13 +142,15 @@ __global__ void __launch_bounds__(kMmaThreads, 2) mma_gemv_kernel(GemvParams p) 
     constexpr int NCH = 2;  // register path for K <= 4096
     if ((k / 8) <= NCH * kMmaThreads && aligned16(p.x)) {
       const uint4 none[NCH] = {};
-      f16 = mgv > 1 ? prep_rows_warp<false>(p.x + m0 * k, nullptr, k, mgv, 0.0f, x_stage, x16, escale, nullptr)
+      f16 = (mgv > 1 || aliased) ? prep_rows_warp<false>(p.x + m0 * k, nullptr, k, mgv, 0.0f, x_stage, x16, escale, nullptr)
                     : prep_rows_regs<NCH, false>(p.x + m0 * k, k, mgv, none, 0.0f, x_stage, x16, escale, redf, redd,
                                                  nullptr);
     } else {
       load_rows_lsu(x_stage, p.x + m0 * k, static_cast<int64_t>(mgv) * k);
       __syncthreads();
-      f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
+      // With one staging buffer the f16 operand would overwrite the BF16 rows
+      // before their exactness is known: the BF16 operand then.
+      f16 = aliased ? false : mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
     }
     NVFP4DA_PHASE(3);
     if (!scales_ready) {

@@ -44,7 +44,7 @@ struct MmaGemvLayout {
   uint32_t s_bytes, xs_bytes, x16_bytes, red_bytes;
   __host__ __device__ uint32_t s_off() const { return 0; }
   __host__ __device__ uint32_t xs_off() const { return s_bytes; }
-  __host__ __device__ uint32_t x16_off() const { return s_bytes + xs_bytes; }
+  __host__ __device__ uint32_t x16_off() const { return x16_bytes ? s_bytes + xs_bytes : s_bytes; }
   __host__ __device__ uint32_t red_off() const { return s_bytes + xs_bytes + x16_bytes; }
   __host__ __device__ uint32_t total() const { return red_off() + red_bytes; }
 };
@@ -56,7 +56,9 @@ __host__ __device__ inline MmaGemvLayout mma_gemv_layout(int rows, int64_t k, in
   const int tile_rows = ((rows + 15) / 16) * 16;
   l.s_bytes = r16(static_cast<uint64_t>(tile_rows) * (k / 16));
   l.xs_bytes = r16(static_cast<uint64_t>(mg) * k * 2);
-  l.x16_bytes = r16(static_cast<uint64_t>(mg) * k * 2);
+  // Several rows on the warp-per-row path (K <= 4096) convert in place: no
+  // separate f16 buffer.
+  l.x16_bytes = (mg > 1 && k <= 4096) ? 0 : r16(static_cast<uint64_t>(mg) * k * 2);
   l.red_bytes = kMmaWarps * 16 * 8 * 4;
   return l;
 }
@@ -511,36 +513,63 @@ __device__ __forceinline__ bool prep_rows_regs(const uint16_t* x, int64_t k, int
 // exact in any order, then the power-of-two f16 operand) with warp reductions
 // only, so the rows proceed in parallel and the CTA meets one barrier in all.
 // Each lane only rereads the 16-byte chunks it wrote itself.  `g` is the norm
-// gain in global memory (read through L1; every warp reads the same chunks).
-// Same outputs as prep_rows_regs.
+// gain, in shared or global memory (every warp reads the same chunks).
+// Same outputs as prep_rows_regs; with x16 == x_stage the two share one
+// buffer (see below).
 template <bool NORM, bool L2_ONLY = false>
 __device__ __forceinline__ bool prep_rows_warp(const uint16_t* x, const uint16_t* g, int64_t k, int mgv, float eps,
                                                uint16_t* x_stage, __half* x16, float* escale, uint16_t* dbg) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int kv8 = static_cast<int>(k / 8);
+  // x16 == x_stage: one buffer, the f16 operand written over the BF16 rows
+  // only once every row is known to convert exactly (else the BF16 rows stay).
+  const bool in_place = reinterpret_cast<const void*>(x16) == reinterpret_cast<const void*>(x_stage);
   int inexact = 0;
   for (int m = warp; m < mgv; m += kMmaWarps) {
     uint4* row = reinterpret_cast<uint4*>(x_stage + m * k);  // this warp's row, staged in shared memory
     const uint4* src = reinterpret_cast<const uint4*>(x + m * k);
-    double ss = 0.0;
-    for (int idx = lane; idx < kv8; idx += 32) {
-      const uint4 v = L2_ONLY ? __ldcg(src + idx) : src[idx];
-      row[idx] = v;
-      if constexpr (NORM) {
-        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    // Four FP64 partial sums (the squares of BF16 values are exact in FP32 and
+    // their FP64 sum is exact, so the order does not change the result).
+    double ssp[4] = {0.0, 0.0, 0.0, 0.0};
+    constexpr int kBatch = 6;  // loads in flight per lane (two rounds at K = 3072)
+    for (int idx0 = lane; idx0 < kv8; idx0 += 32 * kBatch) {
+      uint4 v[kBatch];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float a = __uint_as_float(wv[q] << 16), b = __uint_as_float(wv[q] & 0xffff0000u);
-          ss += static_cast<double>(a * a) + static_cast<double>(b * b);
+      for (int j = 0; j < kBatch; ++j) {
+        const int idx = idx0 + 32 * j;
+        v[j] = idx < kv8 ? (L2_ONLY ? __ldcg(src + idx) : src[idx]) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int idx = idx0 + 32 * j;
+        if (idx < kv8) row[idx] = v[j];
+        if constexpr (NORM) {
+          const uint32_t wv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float a = __uint_as_float(wv[q] << 16), b = __uint_as_float(wv[q] & 0xffff0000u);
+            ssp[q] += static_cast<double>(a * a) + static_cast<double>(b * b);
+          }
         }
       }
     }
+    double ss = (ssp[0] + ssp[1]) + (ssp[2] + ssp[3]);
     float mx = 0.0f;
     if constexpr (NORM) {
       ss = warp_sum_f64(ss);  // also orders the row's shared-memory writes before the reads below
       const float inv = rms_inverse(static_cast<float>(ss), static_cast<float>(k), eps);
-      for (int idx = lane; idx < kv8; idx += 32) {
-        const uint4 v = row[idx], gg = __ldg(reinterpret_cast<const uint4*>(g) + idx);
+      for (int idx0 = lane; idx0 < kv8; idx0 += 32 * kBatch) {
+       uint4 gb[kBatch];
+#pragma unroll
+       for (int j = 0; j < kBatch; ++j) {
+         const int idx = idx0 + 32 * j;
+         gb[j] = idx < kv8 ? reinterpret_cast<const uint4*>(g)[idx] : make_uint4(0u, 0u, 0u, 0u);
+       }
+#pragma unroll
+       for (int j = 0; j < kBatch; ++j) {
+        const int idx = idx0 + 32 * j;
+        if (idx >= kv8) break;
+        const uint4 v = row[idx], gg = gb[j];
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w}, wg[4] = {gg.x, gg.y, gg.z, gg.w};
         uint32_t o[4];
 #pragma unroll
@@ -554,6 +583,7 @@ __device__ __forceinline__ bool prep_rows_warp(const uint16_t* x, const uint16_t
         const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
         row[idx] = nv;
         if (dbg) reinterpret_cast<uint4*>(dbg + m * k)[idx] = nv;
+       }
       }
     } else {
       for (int idx = lane; idx < kv8; idx += 32) {
@@ -586,10 +616,31 @@ __device__ __forceinline__ bool prep_rows_warp(const uint16_t* x, const uint16_t
         inexact |= (__low2float(h) * isc != a) | (__high2float(h) * isc != b);  // round trip gives x back
         o[q] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      reinterpret_cast<uint4*>(x16 + m * k)[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+      if (!in_place) reinterpret_cast<uint4*>(x16 + m * k)[idx] = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
-  return __syncthreads_or(inexact) == 0;
+  const bool exact = __syncthreads_or(inexact) == 0;
+  if (in_place && exact) {
+    // Every row converts exactly: overwrite the BF16 rows with the f16
+    // operand (each lane converts the chunks it owns).
+    for (int m = warp; m < mgv; m += kMmaWarps) {
+      const float sc = 1.0f / escale[m];  // a power of two: exact
+      uint4* row = reinterpret_cast<uint4*>(x_stage + m * k);
+      for (int idx = lane; idx < kv8; idx += 32) {
+        const uint4 v = row[idx];
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const __half2 h = __floats2half2_rn(__uint_as_float(wv[q] << 16) * sc, __uint_as_float(wv[q] & 0xffff0000u) * sc);
+          o[q] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        row[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    __syncthreads();
+  }
+  return exact;
 }
 
 }  // namespace nvfp4da

@@ -136,6 +136,7 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
   uint8_t* s_smem = smem + lay.g.s_off();
   uint16_t* x_stage = reinterpret_cast<uint16_t*>(smem + lay.g.xs_off());
   __half* x16 = reinterpret_cast<__half*>(smem + lay.g.x16_off());
+  const bool aliased = reinterpret_cast<const void*>(x16) == reinterpret_cast<const void*>(x_stage);
   float* mred = reinterpret_cast<float*>(smem + lay.g.red_off());
   uint16_t* gin_s = reinterpret_cast<uint16_t*>(smem + lay.gin_off());
   uint16_t* gq_s = reinterpret_cast<uint16_t*>(smem + lay.gq_off());
@@ -228,7 +229,7 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
         gains_ready = true;
       }
       NVFP4DA_PHASE(4);
-      f16 = mgv > 1 ? prep_rows_warp<true>(p.x + m0 * k, p.g_in, k, mgv, p.eps, x_stage, x16, escale,
+      f16 = (mgv > 1 || aliased) ? prep_rows_warp<true>(p.x + m0 * k, gin_s, k, mgv, p.eps, x_stage, x16, escale,
                                            (p.dbg_xnorm && blockIdx.x == 0) ? p.dbg_xnorm + m0 * k : nullptr)
                     : prep_rows_regs<NCH, true>(p.x + m0 * k, k, mgv, gch, p.eps, x_stage, x16, escale, redf, redd,
                                       (p.dbg_xnorm && blockIdx.x == 0) ? p.dbg_xnorm + m0 * k : nullptr);
@@ -279,7 +280,9 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kMmaThread
         }
         __syncthreads();
       }
-      f16 = mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
+      // With one staging buffer the f16 operand would overwrite the BF16 rows
+      // before their exactness is known: the BF16 operand then.
+      f16 = aliased ? false : mma_prepare_f16(x_stage, x16, k, mgv, escale, red_small);
     }
     NVFP4DA_PHASE(5);
     if (!scales_ready) {
