@@ -19,6 +19,7 @@
 #include "attention.cuh"
 #include "attention_stream.cuh"
 #include "attention_prefill.cuh"
+#include "attention_prefill_tc.cuh"
 #include "elementwise.cuh"
 #include "gemv_kernel.cuh"
 #include "prefill_gemm.cuh"
@@ -510,7 +511,40 @@ int run_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uin
                   int64_t past_length, const int64_t* past_lengths, int64_t max_past, void* ws, size_t ws_bytes,
                   cudaStream_t s, bool pdl, bool clear_counters, int64_t pos_offset = 0,
                   float* out_partial = nullptr) {
-  // Prefill-sized T: the tensor-core kernel (one CTA per 64 query tokens).
+  // Prefill-sized T: tcgen05 flash attention (128 query rows per CTA, TMA
+  // tiles, accumulators in tensor memory).
+  if (tokens >= kPrefillAttnMinT && head_dim == kPtD && !out_partial && pos_offset == 0 && aligned(q, 16) &&
+      aligned(kc, 16) && aligned(vc, 16) && aligned(ctx, 16) && batch <= 65535 && q_heads <= 65535 &&
+      batch * kv_heads * capacity < (int64_t(1) << 31) && batch * tokens < (int64_t(1) << 31) &&
+      tensor_map_encoder() != nullptr) {
+    auto fn = tensor_map_encoder();
+    CUtensorMap tq, tk, tv;
+    const cuuint64_t qdims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(q_heads),
+                                 static_cast<cuuint64_t>(batch * tokens)};
+    const cuuint64_t qstr[2] = {static_cast<cuuint64_t>(head_dim * 2), static_cast<cuuint64_t>(q_heads * head_dim * 2)};
+    const cuuint32_t qbox[3] = {64, 1, static_cast<cuuint32_t>(kPtRows)};
+    const cuuint32_t ones[3] = {1, 1, 1};
+    const int64_t rows = batch * kv_heads * capacity;
+    if (fn(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(q), qdims, qstr, qbox, ones,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+        make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kc, head_dim, rows, head_dim * 2, 64, kPtKeys,
+                    CU_TENSOR_MAP_SWIZZLE_128B) &&
+        make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, vc, head_dim, rows, head_dim * 2, 64, kPtKeys,
+                    CU_TENSOR_MAP_SWIZZLE_128B)) {
+      PrefillTcParams pp{ctx, static_cast<int>(batch), static_cast<int>(tokens), static_cast<int>(q_heads),
+                         static_cast<int>(kv_heads), capacity, past_length, past_lengths,
+                         static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim))), nullptr};
+      cudaError_t e = ensure_smem(attn_prefill_tc_kernel, kPtSmem);
+      if (e != cudaSuccess) return cuda_fail(e, "prefill attention shared-memory opt-in");
+      const dim3 grid(static_cast<unsigned>(ceil_div(tokens, kPtRows)), static_cast<unsigned>(q_heads),
+                      static_cast<unsigned>(batch));
+      attn_prefill_tc_kernel<<<grid, kPtThreads, kPtSmem, s>>>(tq, tk, tv, pp);
+      NVFP4DA_CHECK_LAUNCH("prefill attention launch");
+      return NVFP4DA_OK;
+    }
+  }
+  // Otherwise the mma.sync kernel (one CTA per 64 query tokens).
   if (tokens >= kPrefillAttnMinT && head_dim == kPaD && !out_partial && pos_offset == 0 && aligned(q, 16) &&
       aligned(kc, 16) && aligned(vc, 16) && aligned(ctx, 4) && batch <= 65535 && q_heads <= 65535) {
     PrefillAttnParams pp{q, kc, vc, ctx, batch, tokens, q_heads, kv_heads, capacity, past_length, past_lengths,
