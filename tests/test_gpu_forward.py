@@ -262,3 +262,25 @@ def test_config2_batched_decode_full_size_sampled():
         assert_bitwise(v_seq[0, :, p], st["v_projected"][r].reshape(hkv, d))
         assert_attention_policy(st["context"][r], oracle.gqa_attention(st["q_rope"][r], k_seq, v_seq, p))
         assert_stage_policy(out_bits[r], oracle.w4a16_linear(st["context"][r].reshape(1, 1, hq * d), host_w["o"]))
+
+
+def test_hostio_forward_matches_device_forward():
+    """nvfp4da_decoder_attention_forward_hostio (host input in, forward, host
+    output out in one call) gives the bits of the device-buffer forward."""
+    import nvfp4da_capi
+
+    inp, ws = canonical_inputs()
+    g_in, g_q, g_k = inp.input_norm_weight.cuda(), inp.q_norm_weight.cuda(), inp.k_norm_weight.cuda()
+    expected, _ = run_forward(inp.x.cuda(), g_in, ws, g_q, g_k, inp.k_cache.cuda(), inp.v_cache.cuda(), 511,
+                              stages=False)
+    x = torch.zeros_like(inp.x, device="cuda")
+    out = torch.empty_like(x)
+    fw = nvfp4da_capi.Forward(x, g_in, ws["q"], ws["k"], ws["v"], g_q, g_k, ws["o"], inp.k_cache.cuda(),
+                              inp.v_cache.cuda(), out, past_length=511)
+    x_host = inp.x.pin_memory()
+    out_host = torch.empty_like(inp.x).pin_memory()
+    for _ in range(2):
+        out_host.zero_()
+        fw.run_hostio(x_host, out_host)
+        torch.cuda.synchronize()
+        assert torch.equal(out_host.view(torch.int16), expected.cpu().view(torch.int16))
