@@ -78,12 +78,13 @@ def step_bytes(shape) -> dict:
     return {"qkv": qkv, "attention": attn, "o_proj": o, "step": total}
 
 
-def ncu_traffic(kernel: str) -> float | None:
+def ncu_traffic(kernel: str, summary: str | None = None) -> float | None:
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
-    summary (profiles/<kernel>_canonical.md, line `dram_bytes_per_launch: N`)."""
+    summary (profiles/<kernel>_canonical.md, or profiles/<summary>, line
+    `dram_bytes_per_launch: N`)."""
     import re
 
-    p = ROOT / "profiles" / f"{kernel}_canonical.md"
+    p = ROOT / "profiles" / (summary or f"{kernel}_canonical.md")
     try:
         m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
         return float(m.group(1)) if m else None
@@ -650,6 +651,66 @@ def run_prefill(args) -> None:
     _finish(world)
 
 
+def run_attention_workload(args) -> None:
+    """One attention kernel on its config, timed alone (a separate line, not
+    the default workload): attention-c3 = configs[3] decode attention (B=8,
+    P=32767, C=32768; the streaming kernel, HBM roofline), attention-c4 =
+    configs[4] causal prefill attention (B=4, T=2048; tcgen05, tensor
+    roofline)."""
+    world, rank, local = dist_setup()
+    import nvfp4da_capi as capi
+
+    lib = capi.load()
+    c3 = args.workload == "attention-c3"
+    b, t, hq, hkv, d = (8, 1, 24, 6, 128) if c3 else (4, 2048, 24, 6, 128)
+    cap, past = (32768, 32767) if c3 else (4096, 0)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.randn((b, t, hq, d), generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn((b, hkv, cap, d), generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn((b, hkv, cap, d), generator=g, device="cuda").to(torch.bfloat16)
+    ctx = torch.empty_like(q)
+    wsb = lib.nvfp4da_gqa_attention_workspace_size(b, t, hq, hkv, d, past)
+    ws = torch.zeros(max(wsb, 256), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def call():
+        st = lib.nvfp4da_gqa_attention_cached(q.data_ptr(), k.data_ptr(), v.data_ptr(), ctx.data_ptr(), b, t, hq,
+                                              hkv, cap, d, past, None, past, ws.data_ptr(), wsb, stream.cuda_stream)
+        assert st == 0, lib.nvfp4da_last_error()
+
+    steps = max(3, min(args.steps, 50))
+    ms, _ = _time_steps(call, steps, max(args.warmup, 3), stream, world)
+    ms /= steps
+    if c3:
+        byts = b * (past + 1) * 2 * hkv * d * 2 + 2 * b * hq * d * 2
+        peak, src = measured_peak_gbs()
+        ach = byts / (ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "peak_source": src, "bytes_per_launch": byts,
+                "traffic": ncu_traffic("attn_stream", "attn_stream_configs3.md"),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                  "(profiles/attn_stream_configs3.md)"}
+        metric, value, unit = "configs[3] decode attention HBM GB/s", round(ach, 1), "GB/s"
+    else:
+        fl = 4.0 * b * hq * d * t * (t + 1) / 2
+        try:
+            peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+            src = "measured (MEASURED_PEAKS.json bf16_tflops)"
+        except Exception:
+            peak, src = 1590.0, "fallback 1.59 PFLOP/s"
+        ach = fl / (ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4), "peak_source": src, "flops_per_launch": fl,
+                "flops_note": "the causal half: 4*B*Hq*D*T(T+1)/2"}
+        metric, value, unit = "configs[4] causal prefill attention TFLOP/s", round(ach, 1), "TFLOP/s"
+    if rank == 0:
+        print(json.dumps({"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
+                          "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                          "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v)",
+                          "config": {"workload": args.workload}, "roofline": roof}), flush=True)
+    _finish(world)
+
+
 def run_e2e_hostio(args, reps, stream, world) -> dict:
     """Same metric through the C ABI with host buffers: one library call per
     step copies a pinned host input in, runs the forward and copies the output
@@ -793,13 +854,16 @@ def main() -> None:
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-workloads", action="store_true",
                     help="only the configs[0] line (no configs[2]/[3]/[4] sub-objects)")
-    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
-                    help="decode = configs[0] (the metric's workload); prefill = configs[4], reported separately")
+    ap.add_argument("--workload", choices=("decode", "prefill", "attention-c3", "attention-c4"), default="decode",
+                    help="decode = configs[0] (the metric's workload); prefill = configs[4], reported separately; "
+                         "attention-c3 / attention-c4 = one attention kernel on configs[3] / configs[4]")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload.startswith("attention-"):
+        run_attention_workload(args)
     else:
         run_gpu(args)
 
