@@ -178,12 +178,7 @@ int check_weight(const nvfp4da_weight* w, const char* name) {
 bool gemm_tc_supported(const uint16_t* x, int64_t m, const nvfp4da_weight& w, const uint16_t* y);
 int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s);
 constexpr int64_t kGemmMinMDecl = 64;  // at and above this M the tensor-core GEMM replaces the GEMV
-constexpr int64_t kPrefillMinM = 16;   // at and above this M the forward takes the modular chain
-constexpr int64_t kSplitMaxM = 128;    // up to this M the chain's GEMMs split K (one M tile)
-constexpr size_t kSplitBudget = 4u << 20;  // bytes of split-K partials in the forward's workspace
-int gemm_splits(int64_t m, int64_t n, int64_t k, size_t budget);
-int run_gemm_tc_split(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s,
-                      float* partial, int splits);
+constexpr int64_t kPrefillMinM = 128;  // at and above this M the forward takes the modular chain
 constexpr int64_t kPrefillAttnMinT = 64;  // at and above this T attention runs on the tensor cores
 
 // ---------------------------------------------------------------- GEMV plan
@@ -259,14 +254,7 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStream_t s,
   return cudaErrorInvalidConfiguration;
 }
 
-int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s, bool pdl,
-             float* splitk = nullptr, size_t splitk_bytes = 0) {
-  // Batched decode (M of a few dozen rows): the tensor-core GEMM with K split
-  // over enough CTAs to cover the SMs, when the caller lends partial space.
-  if (splitk && m >= kPrefillMinM && m <= kSplitMaxM && gemm_tc_supported(x, m, w, y)) {
-    const int splits = gemm_splits(m, w.rows, w.cols, splitk_bytes);
-    if (splits >= 2) return run_gemm_tc_split(x, m, w, y, s, splitk, splits);
-  }
+int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s, bool pdl) {
   if (m >= kGemmMinMDecl && gemm_tc_supported(x, m, w, y)) return run_gemm_tc(x, m, w, y, s);
   GemvPlan pl;
   if (!plan_gemv(m, w.rows, w.cols, pl))
@@ -318,49 +306,6 @@ bool gemm_tc_supported(const uint16_t* x, int64_t m, const nvfp4da_weight& w, co
          w.rows <= (int64_t(1) << 31) && tensor_map_encoder() != nullptr;
 }
 
-// Split-K plan of the tensor-core GEMM for a small M: enough CTAs to cover
-// the SMs, the partials within `budget` bytes; 1 split when it does not pay.
-int gemm_splits(int64_t m, int64_t n, int64_t k, size_t budget) {
-  const int64_t tiles = ceil_div(n, kPgBN) * ceil_div(m, kPgBM);
-  const int64_t nk = k / kPgBK;
-  int64_t splits = std::min<int64_t>(ceil_div(sm_count(), tiles), nk / 4);
-  splits = std::min<int64_t>(splits, static_cast<int64_t>(budget / (static_cast<size_t>(m * n) * 4)));
-  if (splits < 2) return 1;
-  const int64_t per = ceil_div(ceil_div(nk, splits), 4) * 4;  // whole scale tiles per split
-  return static_cast<int>(ceil_div(nk, per));
-}
-
-// The GEMM with K split over `splits` CTA layers (partials in `partial`, at
-// least splits * m * n floats), then the ordered reduction.
-int run_gemm_tc_split(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s,
-                      float* partial, int splits) {
-  const int64_t n = w.rows, k = w.cols, nk = k / kPgBK;
-  const int per = static_cast<int>(ceil_div(ceil_div(nk, splits), 4) * 4);
-  splits = static_cast<int>(ceil_div(nk, per));
-  CUtensorMap tx, tw, ts;
-  if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m, k * 2, kPgBK, kPgBM,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed_values, k / 2, n, k / 2, kPgBK / 2, kPgBN,
-                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.block_scales, k / 16, n, k / 16, 16, kPgBN,
-                   CU_TENSOR_MAP_SWIZZLE_NONE))
-    return fail(NVFP4DA_ERR_CUDA, "tensor map encoding failed for the tensor-core GEMM");
-  PgParams p{m, n, k, w.global_decode_scale, y, nullptr, per, partial};
-  auto* kern = w4a16_gemm_tc_kernel<kPgBN>;
-  const uint32_t smem = PgLayout<kPgBN>::total();
-  cudaError_t e = ensure_smem(kern, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM shared-memory opt-in");
-  const dim3 grid(static_cast<unsigned>(ceil_div(n, kPgBN)), static_cast<unsigned>(ceil_div(m, kPgBM)),
-                  static_cast<unsigned>(splits));
-  kern<<<grid, PgCfg<kPgBN>::kThreads, smem, s>>>(tx, tw, ts, p);
-  NVFP4DA_CHECK_LAUNCH("tensor-core GEMM launch");
-  const int64_t mn = m * n;
-  splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(mn, 256)), 256, 0, s>>>(partial, splits, mn,
-                                                                                   w.global_decode_scale, y);
-  NVFP4DA_CHECK_LAUNCH("split-K reduction launch");
-  return NVFP4DA_OK;
-}
-
 int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s) {
   const int64_t n = w.rows, k = w.cols;
   CUtensorMap tx, tw, ts;
@@ -371,7 +316,7 @@ int run_gemm_tc(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t*
       !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.block_scales, k / 16, n, k / 16, 16, kPgBN,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
     return fail(NVFP4DA_ERR_CUDA, "tensor map encoding failed for the tensor-core GEMM");
-  PgParams p{m, n, k, w.global_decode_scale, y, nullptr, static_cast<int>(k / kPgBK), nullptr};
+  PgParams p{m, n, k, w.global_decode_scale, y, nullptr};
   auto* kern = w4a16_gemm_tc_kernel<kPgBN>;
   const uint32_t smem = PgLayout<kPgBN>::total();
   cudaError_t e = ensure_smem(kern, smem);
@@ -721,7 +666,6 @@ struct ForwardLayout {
   QkvPlan qkv;
   AttnPlan attn;
   size_t q_buf, ctx_buf, attn_ws, scratch;  // byte offsets
-  size_t splitk, splitk_bytes;               // split-K partials of the chain's GEMMs (0 bytes: none)
   size_t total;
   // modular-path buffers (offsets)
   size_t xn, qp, kp, vp, qn, kn, kr;
@@ -801,9 +745,6 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
     L.kr = off;
     off += kvact;
   }
-  L.splitk = off;
-  L.splitk_bytes = (!L.fused && m <= kSplitMaxM) ? kSplitBudget : 0;
-  off += L.splitk_bytes;
   L.total = off;
   return NVFP4DA_OK;
 }
@@ -1485,10 +1426,9 @@ int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* 
     uint16_t* kn = buf(st ? st->k_normalized : nullptr, L.kn);
     uint16_t* kr = reinterpret_cast<uint16_t*>(base + L.kr);
     if ((r = nvfp4da_rms_norm(a->x, a->input_norm_weight, xn, m, a->hidden, a->rms_eps, s))) return r;
-    float* sk = L.splitk_bytes ? reinterpret_cast<float*>(base + L.splitk) : nullptr;
-    if ((r = run_gemv(xn, m, a->q_weight, qp, s, false, sk, L.splitk_bytes))) return r;
-    if ((r = run_gemv(xn, m, a->k_weight, kp, s, false, sk, L.splitk_bytes))) return r;
-    if ((r = run_gemv(xn, m, a->v_weight, vp, s, false, sk, L.splitk_bytes))) return r;
+    if ((r = run_gemv(xn, m, a->q_weight, qp, s, false))) return r;
+    if ((r = run_gemv(xn, m, a->k_weight, kp, s, false))) return r;
+    if ((r = run_gemv(xn, m, a->v_weight, vp, s, false))) return r;
     if ((r = nvfp4da_rms_norm(qp, a->q_norm_weight, qn, m * hq, d, a->rms_eps, s))) return r;
     if ((r = nvfp4da_rms_norm(kp, a->k_norm_weight, kn, m * a->kv_heads, d, a->rms_eps, s))) return r;
     auto rope = [&](const uint16_t* in, uint16_t* out, int64_t heads) {
@@ -1508,9 +1448,7 @@ int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* 
                       false, true);
     if (r) return r;
   }
-  if ((r = run_gemv(ctx_buf, m, a->out_weight, a->output, s, L.fused,
-                    L.splitk_bytes ? reinterpret_cast<float*>(base + L.splitk) : nullptr, L.splitk_bytes)))
-    return r;
+  if ((r = run_gemv(ctx_buf, m, a->out_weight, a->output, s, L.fused))) return r;
   return NVFP4DA_OK;
 }
 

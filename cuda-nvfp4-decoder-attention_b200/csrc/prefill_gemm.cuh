@@ -59,23 +59,7 @@ struct PgParams {
   const float* gamma;
   uint16_t* y;  // [M, N]
   unsigned* err;
-  // Split K (small M): CTA z of grid.z takes K steps [z * ksteps, +ksteps)
-  // (ksteps a multiple of 4) and writes its FP32 partial, gamma not applied,
-  // to partial[z][M][N]; splitk_reduce_kernel finishes.  partial == nullptr:
-  // one split, BF16 output.
-  int ksteps;
-  float* partial;
 };
-
-// y = BF16(gamma * sum_z partial[z]) with the splits added in order (FP32,
-// round to nearest): the same bits on every call.
-__global__ void splitk_reduce_kernel(const float* partial, int splits, int64_t mn, const float* gamma, uint16_t* y) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= mn) return;
-  float acc = partial[i];
-  for (int z = 1; z < splits; ++z) acc = __fadd_rn(acc, partial[z * mn + i]);
-  y[i] = f32_to_bf16_bits(__fmul_rn(acc, *gamma));
-}
 
 // Shared-memory layout of one CTA (byte offsets from a 1024-aligned base).
 template <int BN>
@@ -280,10 +264,7 @@ __global__ void __launch_bounds__(PgCfg<BN>::kThreads, 1)
   __shared__ volatile unsigned s_bad;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m0 = blockIdx.y * kPgBM, n0 = blockIdx.x * BN;
-  // K steps of this CTA: [kt0, kt0 + nk) (all of them without split K); the
-  // pipeline below counts local steps, the loads add kt0.
-  const int kt0 = p.partial ? static_cast<int>(blockIdx.z) * p.ksteps : 0;
-  const int nk = p.partial ? min(p.ksteps, static_cast<int>(p.k / kPgBK) - kt0) : static_cast<int>(p.k / kPgBK);
+  const int nk = static_cast<int>(p.k / kPgBK);
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
@@ -318,11 +299,11 @@ __global__ void __launch_bounds__(PgCfg<BN>::kThreads, 1)
         if ((kt & 3) == 0) {
           const int g = kt >> 2;
           mbar_arrive_expect_tx(&bar_sfull[g % kSl], L::kS);
-          tma_load_2d(smem + L::sc(g % kSl), &tm_s, (kt0 / 4 + g) * 16, n0, &bar_sfull[g % kSl]);
+          tma_load_2d(smem + L::sc(g % kSl), &tm_s, g * 16, n0, &bar_sfull[g % kSl]);
         }
         mbar_arrive_expect_tx(&bar_full[st], L::kA + L::kW);
-        tma_load_2d(smem + L::a(st), &tm_x, (kt0 + kt) * kPgBK, m0, &bar_full[st]);
-        tma_load_2d(smem + L::w(st), &tm_w, (kt0 + kt) * (kPgBK / 2), n0, &bar_full[st]);
+        tma_load_2d(smem + L::a(st), &tm_x, kt * kPgBK, m0, &bar_full[st]);
+        tma_load_2d(smem + L::w(st), &tm_w, kt * (kPgBK / 2), n0, &bar_full[st]);
       }
     }
   } else if (warp == 1) {
@@ -402,11 +383,7 @@ __global__ void __launch_bounds__(PgCfg<BN>::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[16 * hh + j] = __float_as_uint(f[j]);
           }
-          if (grow < p.m && p.partial) {
-            float* dst = p.partial + (static_cast<int64_t>(blockIdx.z) * p.m + grow) * p.n + n0 + c0;
-            const int64_t cols = p.n - (n0 + c0);
-            for (int j = 0; j < 32 && j < cols; ++j) dst[j] = __uint_as_float(v[j]);
-          } else if (grow < p.m) {
+          if (grow < p.m) {
             uint16_t* dst = p.y + grow * p.n + n0 + c0;
             const int64_t cols = p.n - (n0 + c0);
             if (cols >= 32 && (p.n % 8) == 0) {
