@@ -161,6 +161,9 @@ def dist_setup():
     if world > 1:
         import torch.distributed as dist
 
+        # NCCL's version banner goes to stdout, where rank 0's JSON line is.
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     else:

@@ -63,43 +63,75 @@ def owner_of(position: int, shards: list[KVShard]) -> int:
 
 
 class CudaStages:
-    """The stages on this rank's GPU through the C ABI (libnvfp4da.so)."""
+    """The stages on this rank's GPU through the C ABI (libnvfp4da.so).
+
+    A decode loop calls the stages with the same tensors every step, so the
+    C argument structs and the intermediate buffers (q, workspace, partials,
+    context) are built once per set of tensors and reused: a step costs one
+    library call per stage and no allocation but its output."""
 
     def __init__(self):
         import nvfp4da_capi
 
         self.capi = nvfp4da_capi
         self.lib = nvfp4da_capi.load()
+        self._front = {}
+        self._part = {}
+        self._ctx = {}
+        self._wo = {}
+
+    @staticmethod
+    def _key(*tensors):
+        return tuple((t.data_ptr(), tuple(t.shape)) for t in tensors)
+
+    @staticmethod
+    def _bounded(cache: dict) -> dict:
+        """Entries keep their tensors alive: forget them all past 16 sets."""
+        if len(cache) >= 16:
+            cache.clear()
+        return cache
 
     def front(self, x, g_in, wq, wk, wv, g_q, g_k, k_shard, v_shard, shard: KVShard, global_capacity: int,
               past_length: int, rms_eps: float, rope_theta: float) -> torch.Tensor:
         capi = self.capi
-        b, t, h = x.shape
-        hkv, d = k_shard.shape[1], k_shard.shape[3]
-        a = capi.ForwardArgs()
-        a.x, a.input_norm_weight = x.data_ptr(), g_in.data_ptr()
-        a.q_weight, a.k_weight, a.v_weight = capi.weight(wq), capi.weight(wk), capi.weight(wv)
-        a.out_weight = capi.weight(wq)  # not used by the front half; any valid [H, H] weight
-        a.q_norm_weight, a.k_norm_weight = g_q.data_ptr(), g_k.data_ptr()
-        a.k_cache, a.v_cache = k_shard.data_ptr(), v_shard.data_ptr()
-        q = torch.empty((b, t, h // d, d), dtype=torch.bfloat16, device=x.device)
-        a.output = q.data_ptr()
-        a.batch, a.tokens, a.hidden, a.kv_heads, a.head_dim, a.capacity = b, t, h, hkv, d, shard.capacity
-        a.past_length, a.past_lengths, a.max_past_length = past_length, None, past_length
+        key = self._key(x, g_in, g_q, g_k, k_shard, v_shard, wq.packed_values, wk.packed_values, wv.packed_values)
+        hit = self._front.get(key)
+        if hit is None:
+            b, t, h = x.shape
+            hkv, d = k_shard.shape[1], k_shard.shape[3]
+            a = capi.ForwardArgs()
+            a.x, a.input_norm_weight = x.data_ptr(), g_in.data_ptr()
+            a.q_weight, a.k_weight, a.v_weight = capi.weight(wq), capi.weight(wk), capi.weight(wv)
+            a.out_weight = capi.weight(wq)  # not used by the front half; any valid [H, H] weight
+            a.q_norm_weight, a.k_norm_weight = g_q.data_ptr(), g_k.data_ptr()
+            a.k_cache, a.v_cache = k_shard.data_ptr(), v_shard.data_ptr()
+            q = torch.empty((b, t, h // d, d), dtype=torch.bfloat16, device=x.device)
+            a.output = q.data_ptr()
+            a.batch, a.tokens, a.hidden, a.kv_heads, a.head_dim, a.capacity = b, t, h, hkv, d, shard.capacity
+            a.past_lengths = None
+            # keep everything the struct points into alive with it
+            hit = self._bounded(self._front)[key] = (a, q, (x, g_in, g_q, g_k, k_shard, v_shard, wq, wk, wv))
+        a, q, _ = hit
+        a.past_length, a.max_past_length = past_length, past_length
         a.rms_eps, a.rope_theta = rms_eps, rope_theta
         st = self.lib.nvfp4da_qkv_rope_append_shard(C.byref(a), shard.start, global_capacity, q.data_ptr(),
                                                     torch.cuda.current_stream().cuda_stream)
-        capi._check(st)
+        self.capi._check(st)
         return q
 
     def partials(self, q, k_shard, v_shard, shard: KVShard, past_length: int) -> torch.Tensor:
         b, t, hq, d = q.shape
         hkv = k_shard.shape[1]
         lib = self.lib
-        wsb = lib.nvfp4da_gqa_attention_partials_workspace_size(b, t, hq, hkv, d, shard.start, shard.capacity,
-                                                                past_length)
-        ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=q.device)
-        part = torch.empty((b * t * hq, d + 2), dtype=torch.float32, device=q.device)
+        key = self._key(q, k_shard, v_shard) + ((shard.start, shard.capacity, past_length),)
+        hit = self._part.get(key)
+        if hit is None:
+            wsb = lib.nvfp4da_gqa_attention_partials_workspace_size(b, t, hq, hkv, d, shard.start, shard.capacity,
+                                                                    past_length)
+            ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=q.device)
+            part = torch.empty((b * t * hq, d + 2), dtype=torch.float32, device=q.device)
+            hit = self._bounded(self._part)[key] = (ws, part, (q, k_shard, v_shard))
+        ws, part, _ = hit
         st = lib.nvfp4da_gqa_attention_partials(q.data_ptr(), k_shard.data_ptr(), v_shard.data_ptr(),
                                                 part.data_ptr(), b, t, hq, hkv, shard.capacity, d, shard.start,
                                                 past_length, None, past_length, ws.data_ptr(), ws.numel(),
@@ -109,7 +141,10 @@ class CudaStages:
 
     def combine(self, gathered: torch.Tensor, out_shape) -> torch.Tensor:
         shards, rows, d2 = gathered.shape
-        ctx = torch.empty(out_shape, dtype=torch.bfloat16, device=gathered.device)
+        key = self._key(gathered) + (tuple(out_shape),)
+        ctx = self._ctx.get(key)
+        if ctx is None:
+            ctx = self._bounded(self._ctx)[key] = torch.empty(out_shape, dtype=torch.bfloat16, device=gathered.device)
         st = self.lib.nvfp4da_attention_combine(gathered.data_ptr(), shards, rows, d2 - 2, ctx.data_ptr(),
                                                 torch.cuda.current_stream().cuda_stream)
         self.capi._check(st)
@@ -117,7 +152,15 @@ class CudaStages:
 
     def o_proj(self, ctx: torch.Tensor, wo) -> torch.Tensor:
         b, t, hq, d = ctx.shape
-        return self.capi.w4a16_linear(ctx.reshape(b, t, hq * d), wo)
+        key = (wo.packed_values.data_ptr(), wo.block_scales.data_ptr(), wo.global_decode_scale.data_ptr())
+        wt = self._wo.get(key)
+        if wt is None:
+            wt = self._bounded(self._wo)[key] = (self.capi.weight(wo), wo)
+        y = torch.empty((b, t, hq * d), dtype=torch.bfloat16, device=ctx.device)
+        st = self.lib.nvfp4da_w4a16_linear(ctx.data_ptr(), b * t, C.byref(wt[0]), y.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream)
+        self.capi._check(st)
+        return y
 
 
 class ShardedDecoderAttention:
@@ -133,6 +176,7 @@ class ShardedDecoderAttention:
         self.shards = shard_ranges(self.global_capacity, self.world)
         self.shard = self.shards[self.rank]
         self.stages = stages if stages is not None else CudaStages()
+        self._gather = None  # all-gather buffer, reused while the partials' shape stays
 
     def forward_(self, x, input_norm_weight, q_weight, k_weight, v_weight, q_norm_weight, k_norm_weight,
                  out_weight, k_shard, v_shard, past_length: int, *, rms_eps: float = 1e-6,
@@ -149,7 +193,10 @@ class ShardedDecoderAttention:
                      v_shard, self.shard, self.global_capacity, past_length, rms_eps, rope_theta)
         part = st.partials(q, k_shard, v_shard, self.shard, past_length)
         if self.world > 1:
-            flat = torch.empty((self.world * part.shape[0], part.shape[1]), dtype=part.dtype, device=part.device)
+            shape = (self.world * part.shape[0], part.shape[1])
+            flat = self._gather
+            if flat is None or tuple(flat.shape) != shape or flat.device != part.device:
+                flat = self._gather = torch.empty(shape, dtype=part.dtype, device=part.device)
             dist.all_gather_into_tensor(flat, part.contiguous(), group=self.group)
             gathered = flat.view(self.world, *part.shape)
         else:
