@@ -938,9 +938,20 @@ unsigned* step_slot(cudaStream_t stream, unsigned long long** tagged = nullptr) 
   return hit.slot;
 }
 
-const void* step_kernel_ptr(int epl, int gh) {
+// xi: the activation rows in the parameter block (instantiated for D = 128).
+const void* step_kernel_ptr(int epl, int gh, bool xi = false) {
+  if (xi) {
+    if (epl != 4) return nullptr;
+    switch (gh) {
+      case 1: return reinterpret_cast<const void*>(decode_step_kernel<4, 1, true>);
+      case 2: return reinterpret_cast<const void*>(decode_step_kernel<4, 2, true>);
+      case 4: return reinterpret_cast<const void*>(decode_step_kernel<4, 4, true>);
+      case 8: return reinterpret_cast<const void*>(decode_step_kernel<4, 8, true>);
+      default: return nullptr;
+    }
+  }
 #define NVFP4DA_STEP_CASE(E, G) \
-  if (epl == E && gh == G) return reinterpret_cast<const void*>(decode_step_kernel<E, G>);
+  if (epl == E && gh == G) return reinterpret_cast<const void*>(decode_step_kernel<E, G, false>);
   NVFP4DA_STEP_CASE(2, 1)
   NVFP4DA_STEP_CASE(2, 2)
   NVFP4DA_STEP_CASE(2, 4)
@@ -966,7 +977,8 @@ struct StepPlan {
   uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
   int o_predecode, od_ld;
   uint32_t off_od;
-  size_t proj, ctx, part_o, part_ml, total;  // workspace offsets / bytes
+  size_t proj, ctx, part_o, part_ml, xin, total;
+  static constexpr size_t kNoWords = ~size_t(0);  // workspace offsets / bytes
 };
 
 // Static shared memory of a step-kernel instantiation (cached per device).
@@ -1109,13 +1121,27 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   s.part_ml = w;
   w += static_cast<size_t>(items) * splits * 2;
   if (w > kStepTagWords) return false;
+  // Activation rows read from host memory (host-buffer entry point), where
+  // the region has room for them after the partials.
+  s.xin = w + static_cast<size_t>(nb * k / 2) <= kStepTagWords ? w : StepPlan::kNoWords;
   s.total = 256;  // the step keeps nothing in the caller's workspace
   return true;
 }
 
+// Whether the step can carry the activation rows of `a` in its parameter block.
+bool step_inline_ok(const nvfp4da_forward_args* a, const StepPlan& pl) {
+  return a->batch * a->tokens * a->hidden <= kStepInlineX && step_kernel_ptr(pl.epl, pl.gh, true) != nullptr;
+}
+
+// x_inline: host copy of the activation rows to send in the parameter block
+// (step_inline_ok must hold), or nullptr to read a->x.
+// x_mapped: the device address of activation rows in mapped page-locked host
+// memory, read by the kernel itself, or nullptr.
 int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaStream_t stream, unsigned* slot,
-             unsigned long long* tagged) {
-  StepParams p{};
+             unsigned long long* tagged, const uint16_t* x_inline = nullptr, const uint16_t* x_mapped = nullptr) {
+  thread_local StepLaunch<true> inl;  // the parameter block with room for inline rows
+  StepParams& p = inl.p;
+  p = StepParams{};
   p.x = a->x;
   p.g_in = a->input_norm_weight;
   const nvfp4da_weight* w4[4] = {&a->q_weight, &a->k_weight, &a->v_weight, &a->out_weight};
@@ -1153,6 +1179,8 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   p.ctx = tagged + pl.ctx;
   p.part_o = tagged + pl.part_o;
   p.part_ml = tagged + pl.part_ml;
+  p.xin = x_mapped ? tagged + pl.xin : nullptr;
+  p.x_mapped = x_mapped;
   p.tag_words = kStepTagWords;
   p.sync = slot;
   p.timeout_ns = 500ull * 1000 * 1000;
@@ -1182,7 +1210,8 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
     const float* den = rope_denominators(a->head_dim, a->rope_theta);
     for (int64_t m = 0; m < a->head_dim / 2; ++m) p.rope_host[m] = make_float2(den[m], 0.0f);
   }
-  const void* fn = step_kernel_ptr(pl.epl, pl.gh);
+  const void* fn = step_kernel_ptr(pl.epl, pl.gh, x_inline != nullptr);
+  if (x_inline) std::memcpy(inl.x, x_inline, static_cast<size_t>(a->batch * a->tokens * a->hidden) * 2);
   cudaError_t e = ensure_smem(fn, pl.smem);
   if (e != cudaSuccess) return cuda_fail(e, "step kernel shared-memory opt-in");
   cudaLaunchConfig_t cfg = {};
@@ -1195,7 +1224,8 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  void* kargs[] = {&p};
+  // StepLaunch<false> is StepParams alone, so &p serves both instantiations.
+  void* kargs[] = {x_inline ? static_cast<void*>(&inl) : static_cast<void*>(&p)};
   e = cudaLaunchKernelExC(&cfg, fn, kargs);
   if (e != cudaSuccess) return cuda_fail(e, "decode step launch");
   return NVFP4DA_OK;
@@ -1366,8 +1396,31 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* a, void* ws, s
   return nvfp4da_decoder_attention_forward_path(a, ws, ws_bytes, stream, NVFP4DA_PATH_AUTO);
 }
 
-int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* ws, size_t ws_bytes, void* stream,
-                                           int path) {
+}  // extern "C"
+
+namespace nvfp4da {
+namespace {
+// The device address of page-locked host memory that the device can address
+// (16-byte aligned), else nullptr.  Asked on every call (well under a
+// microsecond): a cached answer could outlive the buffer's registration.
+void* mapped_address(const void* host) {
+  cudaPointerAttributes at{};
+  void* dev = nullptr;
+  if (cudaPointerGetAttributes(&at, host) == cudaSuccess && at.type == cudaMemoryTypeHost && at.devicePointer &&
+      aligned(at.devicePointer, 16))
+    dev = at.devicePointer;
+  cudaGetLastError();
+  return dev;
+}
+
+// The forward.  x_host (the host-buffer entry point): the activation rows in
+// host memory, and x_host_dev their device address when they are mapped
+// page-locked memory (else nullptr).  On the one-kernel step the rows travel
+// in the launch's parameter block when they fit (6 KB), else the kernel reads
+// them from mapped memory; every other case copies them into a->x on the
+// stream first (a copy-engine transfer, ~10 us of stream time on B200).
+int forward_impl(const nvfp4da_forward_args* a, void* ws, size_t ws_bytes, void* stream, int path,
+                 const uint16_t* x_host, const uint16_t* x_host_dev) {
   int r = check_forward(a);
   if (r) return r;
   if (path != NVFP4DA_PATH_AUTO && path != NVFP4DA_PATH_CHAIN && path != NVFP4DA_PATH_STEP)
@@ -1395,7 +1448,15 @@ int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* 
   if (!ws || ws_bytes < need)
     return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace too small (%zu < %zu bytes)", ws_bytes, need);
   if (!aligned(ws, 256)) return fail(NVFP4DA_ERR_WORKSPACE, "forward workspace must be 256-byte aligned");
-  if (step_ok) return run_step(a, sp, ws, s, slot, tagged);
+  const bool inline_x = x_host && step_ok && step_inline_ok(a, sp);
+  const bool mapped_x = !inline_x && x_host_dev && step_ok && sp.xin != StepPlan::kNoWords;
+  if (x_host && !inline_x && !mapped_x) {
+    const size_t bytes = static_cast<size_t>(a->batch * a->tokens * a->hidden) * 2;
+    cudaError_t e = cudaMemcpyAsync(const_cast<uint16_t*>(a->x), x_host, bytes, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e, "forward_hostio: input copy");
+  }
+  if (step_ok)
+    return run_step(a, sp, ws, s, slot, tagged, inline_x ? x_host : nullptr, mapped_x ? x_host_dev : nullptr);
   char* base = static_cast<char*>(ws);
   const nvfp4da_forward_stages* st = a->stages;
   const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens, d = a->head_dim;
@@ -1450,6 +1511,15 @@ int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* 
   }
   if ((r = run_gemv(ctx_buf, m, a->out_weight, a->output, s, L.fused))) return r;
   return NVFP4DA_OK;
+}
+}  // namespace
+}  // namespace nvfp4da
+
+extern "C" {
+
+int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* a, void* ws, size_t ws_bytes, void* stream,
+                                           int path) {
+  return forward_impl(a, ws, ws_bytes, stream, path, nullptr, nullptr);
 }
 
 int nvfp4da_forward_sync_status(void* stream, unsigned* flags, int clear) {
@@ -1598,31 +1668,19 @@ int nvfp4da_decoder_attention_forward_hostio(const nvfp4da_forward_args* a, cons
   if (r) return r;
   const size_t bytes = static_cast<size_t>(a->batch * a->tokens * a->hidden) * 2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemcpyAsync(const_cast<uint16_t*>(a->x), x_host, bytes, cudaMemcpyHostToDevice, s);
-  if (e != cudaSuccess) return cuda_fail(e, "forward_hostio: input copy");
-  // Output into page-locked host memory that the device can address: the
-  // forward's last kernel writes it directly (posted writes, visible once the
-  // stream reaches this point), which saves a copy-engine round trip.  The
-  // answer for the last buffer is kept per host thread.
-  thread_local const void* last_host = nullptr;
-  thread_local void* last_dev = nullptr;
-  if (output_host != last_host) {
-    cudaPointerAttributes at{};
-    void* dev = nullptr;
-    if (cudaPointerGetAttributes(&at, output_host) == cudaSuccess && at.type == cudaMemoryTypeHost &&
-        at.devicePointer && aligned(at.devicePointer, 16))
-      dev = at.devicePointer;
-    cudaGetLastError();
-    last_host = output_host;
-    last_dev = dev;
-  }
-  if (last_dev) {
+  // Input: see forward_impl (parameter block, mapped read or copy).  Output:
+  // into page-locked host memory that the device can address, the last
+  // kernel stores it directly (visible once the stream reaches this point),
+  // which saves a copy-engine round trip; other buffers are copied.
+  const uint16_t* x_dev = static_cast<const uint16_t*>(mapped_address(x_host));
+  uint16_t* out_dev = static_cast<uint16_t*>(mapped_address(output_host));
+  if (out_dev) {
     nvfp4da_forward_args direct = *a;
-    direct.output = static_cast<uint16_t*>(last_dev);
-    return nvfp4da_decoder_attention_forward(&direct, workspace, workspace_bytes, stream);
+    direct.output = out_dev;
+    return forward_impl(&direct, workspace, workspace_bytes, stream, NVFP4DA_PATH_AUTO, x_host, x_dev);
   }
-  if ((r = nvfp4da_decoder_attention_forward(a, workspace, workspace_bytes, stream))) return r;
-  e = cudaMemcpyAsync(output_host, a->output, bytes, cudaMemcpyDeviceToHost, s);
+  if ((r = forward_impl(a, workspace, workspace_bytes, stream, NVFP4DA_PATH_AUTO, x_host, x_dev))) return r;
+  cudaError_t e = cudaMemcpyAsync(output_host, a->output, bytes, cudaMemcpyDeviceToHost, s);
   if (e != cudaSuccess) return cuda_fail(e, "forward_hostio: output copy");
   return NVFP4DA_OK;
 }

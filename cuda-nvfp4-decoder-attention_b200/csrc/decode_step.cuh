@@ -84,6 +84,12 @@ struct StepParams {
   unsigned long long* ctx;      // [B, H / 2]              context, BF16 pairs
   unsigned long long* part_o;   // [B * Hq, splits, D]     FP32
   unsigned long long* part_ml;  // [B * Hq, splits, 2]     FP32 (m, l)
+  unsigned long long* xin;      // [B, H / 2]              activation rows read from host memory, BF16 pairs
+  // Activation rows in page-locked host memory mapped into the device's
+  // address space, or nullptr (then x).  Each CTA reads a slice of them over
+  // the host link once and publishes it as tagged words (xin); the QKV CTAs
+  // poll the whole rows from L2.  One host read per byte, no copy engine.
+  const uint16_t* x_mapped;
   size_t tag_words;             // the region's size, cleared when the epoch wraps
   unsigned* sync;    // slot
   unsigned long long timeout_ns;
@@ -101,6 +107,21 @@ struct StepParams {
   // (per-sequence lengths read on the device).
   int rope_host_ok;
   float2 rope_host[kMaxHeadDim / 2];
+};
+
+// The launch's parameter block.  With XI the activation rows travel inside
+// it (the host-buffer entry point copies them there on the host), so a step
+// whose input starts in host memory needs no copy-engine transfer before the
+// kernel: the rows reach every SM through the constant cache with the launch.
+constexpr int kStepInlineX = 3072;  // activation elements (6 KB; a 16 KB block measured 2 us slower)
+template <bool XI>
+struct StepLaunch {
+  StepParams p;
+};
+template <>
+struct StepLaunch<true> {
+  StepParams p;
+  uint4 x[kStepInlineX / 8];
 };
 
 // ---------------------------------------------------------------- sync primitives
@@ -287,8 +308,16 @@ __device__ __forceinline__ void mma_pass_decoded(const __half* a_smem, int ld, c
 }
 
 // ---------------------------------------------------------------- the kernel
-template <int EPL, int GH>
-__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
+template <int EPL, int GH, bool XI>
+__global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ StepLaunch<XI> launch) {
+  const StepParams& p = launch.p;
+  // Activation rows: global memory, or (XI) the parameter block itself, read
+  // with generic loads through the parameter space's address.
+  const uint16_t* xin;
+  if constexpr (XI)
+    xin = reinterpret_cast<const uint16_t*>(launch.x);
+  else
+    xin = p.x;
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ uint64_t bar_qkv, bar_kv, bar_o;
   __shared__ float redf[2 * kStepWarps];
@@ -391,6 +420,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   uint32_t epoch;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(epoch) : "l"(sync + kSyncEpoch) : "memory");
   const uint32_t tag = epoch + 1u;
+  // ---- activation rows from host memory: this CTA's 16-byte chunks, read by
+  // the last warp (warp 0's thread 0 has the bulk copies to issue).
+  if (p.x_mapped != nullptr && warp == kStepWarps - 1) {
+    const int64_t n16 = nb * k / 8;
+    const int64_t per = (n16 + gridDim.x - 1) / gridDim.x;
+    const int64_t c_end = (cta + 1) * per < n16 ? (cta + 1) * per : n16;
+    for (int64_t c = cta * per + lane; c < c_end; c += 32) {
+      const uint4 v = reinterpret_cast<const uint4*>(p.x_mapped)[c];
+      st_tagged(p.xin + 4 * c + 0, v.x, tag);
+      st_tagged(p.xin + 4 * c + 1, v.y, tag);
+      st_tagged(p.xin + 4 * c + 2, v.z, tag);
+      st_tagged(p.xin + 4 * c + 3, v.w, tag);
+    }
+  }
   // ---- the activation rows and the input-norm gain first: they head the
   // critical path, so their requests go out before any bulk traffic.
   constexpr int NCH = 2;
@@ -399,8 +442,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   for (int c = 0; c < NCH; ++c) {
     const int idx = threadIdx.x + c * kStepThreads;
     gch[c] = idx < k / 8 ? ldg_stream(p.g_in + 8 * idx) : make_uint4(0u, 0u, 0u, 0u);
-    if (idx < k / 8)
-      for (int m = 0; m < mrows; ++m) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + m * k + 8 * idx));
+    if (!XI && p.x_mapped == nullptr && idx < k / 8)
+      for (int m = 0; m < mrows; ++m) asm volatile("prefetch.global.L2 [%0];" ::"l"(xin + m * k + 8 * idx));
   }
 
   __syncthreads();
@@ -455,8 +498,29 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   // ---- input RMSNorm of the activation rows -> MMA operand, QKV GEMV
   if (has_qkv) {
-    bool f16 = mrows > 1 ? prep_rows_warp<true>(p.x, p.g_in, k, mrows, p.eps, x_stage, x16, escale, nullptr)
-                         : prep_rows_regs<NCH, true>(p.x, k, mrows, gch, p.eps, x_stage, x16, escale, redf, redd, nullptr);
+    if (p.x_mapped != nullptr) {
+      // Every CTA's published slice of the rows, into x_stage (the prep
+      // functions below read their input before writing x_stage).
+      const int pairs = static_cast<int>(nb * k / 2);
+      uint32_t* xs2 = reinterpret_cast<uint32_t*>(x_stage);
+      for (int i0 = threadIdx.x; i0 < pairs; i0 += 8 * kStepThreads) {
+        const unsigned long long* src[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + j * kStepThreads;
+          src[j] = p.xin + (i < pairs ? i : i0);
+        }
+        uint32_t v[8];
+        poll_tagged<8>(src, v, tag, deadline, err);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i0 + j * kStepThreads < pairs) xs2[i0 + j * kStepThreads] = v[j];
+      }
+      __syncthreads();
+      xin = x_stage;
+    }
+    bool f16 = mrows > 1 ? prep_rows_warp<true>(xin, p.g_in, k, mrows, p.eps, x_stage, x16, escale, nullptr)
+                         : prep_rows_regs<NCH, true>(xin, k, mrows, gch, p.eps, x_stage, x16, escale, redf, redd, nullptr);
     NVFP4DA_PHASE(2);
     mbar_spin_until(&bar_qkv, 0, deadline, err);
     if (threadIdx.x == 0) {
@@ -877,10 +941,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         mma_gemv_pass_smem<false, 4>(ow_smem, os_smem, x_stage, k, p.o_tile_rows, o_valid, mrows, mred, outv);
     }
     const float gamma = gamma_o;
-    for (int i = threadIdx.x; i < o_valid * mrows; i += kStepThreads) {
-      const int n = i / o_valid, r = i % o_valid;
-      const float v = f16 ? outv[r * 8 + n] * escale[n] : outv[r * 8 + n];
-      p.out[n * k + orow0 + r] = f32_to_bf16_bits(__fmul_rn(v, gamma));
+    // Eight rows per 16-byte store (o_valid and orow0 are multiples of 8).
+    const int o_oct = o_valid / 8;
+    for (int i = threadIdx.x; i < o_oct * mrows; i += kStepThreads) {
+      const int n = i / o_oct, r0 = (i % o_oct) * 8;
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v0 = outv[(r0 + 2 * j) * 8 + n], v1 = outv[(r0 + 2 * j + 1) * 8 + n];
+        if (f16) {
+          v0 *= escale[n];
+          v1 *= escale[n];
+        }
+        w[j] = static_cast<uint32_t>(f32_to_bf16_bits(__fmul_rn(v0, gamma))) |
+               (static_cast<uint32_t>(f32_to_bf16_bits(__fmul_rn(v1, gamma))) << 16);
+      }
+      *reinterpret_cast<uint4*>(p.out + n * k + orow0 + r0) = make_uint4(w[0], w[1], w[2], w[3]);
     }
     NVFP4DA_PHASE(12);
   }

@@ -184,14 +184,19 @@ int nvfp4da_decoder_attention_forward(const nvfp4da_forward_args* args, void* wo
 int nvfp4da_decoder_attention_forward_path(const nvfp4da_forward_args* args, void* workspace, size_t workspace_bytes,
                                            void* stream, int path);
 /* The forward with host buffers, for hosts that keep activations in host
- * memory: copies x_host ([B, T, H] BF16, ideally pinned) into args->x,
- * runs nvfp4da_decoder_attention_forward, and copies args->output into
- * output_host, all enqueued on `stream` (the caller synchronises before
- * reading output_host).  When output_host is page-locked memory the device
- * can address (cudaHostAlloc / cudaHostRegister, as torch's pin_memory()),
- * the forward writes it directly and args->output is not written.  Replaces the host-side sequence around
- * cuda_decoder_attention_forward_ (decoder_attention_cuda.py:149-417: the
- * caller's x.to(device) and y.cpu()) with one call. */
+ * memory: x_host ([B, T, H] BF16) in, output_host out, all enqueued on
+ * `stream` (the caller synchronises before reading output_host).
+ * Input: when the one-kernel step runs, rows of up to 6 KB travel in the
+ * kernel's parameter block (x_host is read during the call and may be reused
+ * at once; any host memory); larger rows in page-locked memory the device can
+ * address (cudaHostAlloc / cudaHostRegister, as torch's pin_memory()) are
+ * read by the kernel itself; otherwise x_host is copied into args->x on the
+ * stream (and must stay valid until the stream gets there).  Output: into
+ * such page-locked memory the forward writes directly and args->output is
+ * not written; otherwise args->output is copied to output_host.  Replaces
+ * the host-side sequence around cuda_decoder_attention_forward_
+ * (decoder_attention_cuda.py:149-417: the caller's x.to(device) and y.cpu())
+ * with one call. */
 int nvfp4da_decoder_attention_forward_hostio(const nvfp4da_forward_args* args, const uint16_t* x_host,
                                              uint16_t* output_host, void* workspace, size_t workspace_bytes,
                                              void* stream);

@@ -274,3 +274,40 @@ def test_bounded_wait_gives_up_and_reports():
     assert nvfp4da_capi.wait_timeout_probe(2_000_000) == 1  # 2 ms limit
     x = torch.ones(4, device="cuda")
     assert float((x + 1).sum()) == 8.0
+
+
+@pytest.mark.parametrize("b,h,x_kind,out_kind", [
+    (1, 3072, "pinned", "pinned"),      # rows in the parameter block
+    (1, 3072, "pageable", "pinned"),    # parameter block: any host memory
+    (2, 3072, "pinned", "pinned"),      # 12 KB: read by the kernel from mapped memory
+    (2, 3072, "pageable", "pageable"),  # copied in, copied out
+    (1, 1024, "pinned", "pageable"),    # parameter block in, output copied out
+])
+def test_hostio_input_routes_match_the_device_forward(b, h, x_kind, out_kind):
+    """nvfp4da_decoder_attention_forward_hostio on the one-kernel step: the
+    activation rows reach the kernel through its parameter block, through
+    mapped page-locked memory, or by a copy, and the output is written to
+    mapped memory or copied; every route gives the device forward's bits."""
+    import nvfp4da_capi
+
+    pasts = tuple(range(300, 300 + b))
+    inp, host_w = make_case(b, h, max(1, h // 512), 128, pasts if b > 1 else pasts[0], 512, seed=77 + b + h)
+    ws = {k: dev_weight(s) for k, s in host_w.items()}
+    fw, out = forward(inp, ws, pasts if b > 1 else pasts[0], inp.k_cache.cuda(), inp.v_cache.cuda(),
+                      nvfp4da_capi.PATH_AUTO)
+    assert fw.step_supported
+    fw.run()
+    expected = host_bits(out)
+    x_host = inp.x.clone()
+    out_host = torch.empty_like(inp.x)
+    if x_kind == "pinned":
+        x_host = x_host.pin_memory()
+    if out_kind == "pinned":
+        out_host = out_host.pin_memory()
+    fw._keep[0].zero_()  # the device rows: only the copy route writes them again
+    for _ in range(2):
+        out_host.zero_()
+        fw.run_hostio(x_host, out_host)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(host_bits(out_host), expected)
+    assert nvfp4da_capi.sync_status() == 0
