@@ -284,7 +284,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     const int half = (warp - 2) / 4;  // keys [32 half, +32) of each tile, output columns [64 half, +64)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const int64_t pos = pb + t0 + row;  // this row's position (rows past T are computed, not stored)
-    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 1.0f;
+    constexpr float kLog2e = 1.4426950408889634f;
+    float m_run = -INFINITY, ml_run = 0.0f, l_run = 0.0f, alpha_prev = 1.0f;
     float o[kHalfD];
 #pragma unroll
     for (int i = 0; i < kHalfD; ++i) o[i] = 0.0f;
@@ -360,7 +361,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       if (!__all_sync(0xffffffffu, ok)) break;
       mx = fmaxf(mx, s_rowmax[j & 1][half ^ 1][row]);
       const float m_new = fmaxf(m_run, mx);
-      const float alpha = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+      // exp(s - m) as 2^(s log2(e) - m log2(e)) with one rounding in the
+      // exponent: the rounding of m log2(e) is the same for every term of
+      // the row and for alpha, so it cancels in sum(p v) / sum(p).
+      const float ml_new = m_new == -INFINITY ? 0.0f : __fmul_rn(m_new, kLog2e);
+      const float alpha = m_run == -INFINITY ? 0.0f : exp2f(__fsub_rn(ml_run, ml_new));
       // The P buffers are free once PV_{j-1} is done, which the fold of
       // O_{j-1} waits for.
       if (j >= 1 && !(ok = fold(j - 1, alpha_prev))) break;
@@ -374,8 +379,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float s0 = sc[8 * h8 + 2 * e], s1 = sc[8 * h8 + 2 * e + 1];
-            float r0 = s0 == -INFINITY ? 0.0f : expf(s0 - m_new);
-            float r1 = s1 == -INFINITY ? 0.0f : expf(s1 - m_new);
+            float r0 = s0 == -INFINITY ? 0.0f : exp2f(fmaf(s0, kLog2e, -ml_new));
+            float r1 = s1 == -INFINITY ? 0.0f : exp2f(fmaf(s1, kLog2e, -ml_new));
             lsum += r0 + r1;
 #pragma unroll
             for (int term = 0; term < 3; ++term) {
@@ -396,6 +401,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       if (lane == 0) mbar_arrive(&bar_s_empty[sb]);
       l_run = fmaf(l_run, alpha, lsum);
       m_run = m_new;
+      ml_run = ml_new;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_p_full);
