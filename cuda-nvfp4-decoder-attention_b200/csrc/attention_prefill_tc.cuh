@@ -38,7 +38,8 @@
 #include <cuda.h>
 
 #include "common.cuh"
-#include "prefill_gemm.cuh"  // tcgen05 / TMA primitives, pg_wait, mbar_arrive
+#include "attention_prefill.cuh"  // pack_bf16
+#include "prefill_gemm.cuh"       // tcgen05 / TMA primitives, pg_wait, mbar_arrive
 
 namespace nvfp4da {
 
@@ -290,15 +291,13 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 #pragma unroll
     for (int i = 0; i < kHalfD; ++i) o[i] = 0.0f;
     bool ok = true;
-    // Fold O_i (scaled to m_i) into the register accumulator: o = o * a, then
-    // each 16-key step's accumulator added with round-to-nearest;
-    // a = exp(m_{i-1} - m_i).
+    // Fold O_i (scaled to m_i) into the register accumulator: o = o * a +
+    // (first 32-key block), one rounding, then the second block added with
+    // round-to-nearest; a = exp(m_{i-1} - m_i).
     auto fold = [&](int i, float a) -> bool {
       const bool good = pg_wait(&bar_o_full[0], i & 1, &s_bad, p.err);
       if (!__all_sync(0xffffffffu, good)) return false;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-      for (int e = 0; e < kHalfD; ++e) o[e] = __fmul_rn(o[e], a);
 #pragma unroll
       for (int ob = 0; ob < kPtKeys / kPtOBlockKeys; ++ob) {  // this half's 64 columns: four loads, one wait
         uint32_t v[4][16];
@@ -310,7 +309,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[16 * q + e] = __fadd_rn(o[16 * q + e], __uint_as_float(v[q][e]));
+          for (int e = 0; e < 16; ++e)
+            o[16 * q + e] = ob == 0 ? fmaf(o[16 * q + e], a, __uint_as_float(v[q][e]))
+                                    : __fadd_rn(o[16 * q + e], __uint_as_float(v[q][e]));
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -384,10 +385,12 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             lsum += r0 + r1;
 #pragma unroll
             for (int term = 0; term < 3; ++term) {
-              const uint32_t hb = f32_to_bf16_bits(r0), hb1 = f32_to_bf16_bits(r1);
-              w[term][e] = hb | (hb1 << 16);
-              r0 -= __uint_as_float(hb << 16);  // exact residuals
-              r1 -= __uint_as_float(hb1 << 16);
+              const uint32_t both = pack_bf16(r0, r1);  // one conversion for the pair
+              w[term][e] = both;
+              if (term < 2) {
+                r0 -= __uint_as_float(both << 16);  // exact residuals
+                r1 -= __uint_as_float(both & 0xffff0000u);
+              }
             }
           }
 #pragma unroll
