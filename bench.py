@@ -78,18 +78,37 @@ def step_bytes(shape) -> dict:
     return {"qkv": qkv, "attention": attn, "o_proj": o, "step": total}
 
 
+def kernel_source_digest() -> str:
+    """First 16 hex digits of the SHA-256 over the kernel sources (every
+    csrc/*.cuh, in name order): a profile captured from other sources no
+    longer describes the kernels that run."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for f in sorted((PKG / "csrc").glob("*.cuh")):
+        h.update(f.name.encode())
+        h.update(f.read_bytes())
+    return h.hexdigest()[:16]
+
+
 def ncu_traffic(kernel: str, summary: str | None = None) -> float | None:
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
     summary (profiles/<kernel>_canonical.md, or profiles/<summary>, line
-    `dram_bytes_per_launch: N`)."""
+    `dram_bytes_per_launch: N`), or None when the summary's
+    `kernel_sources: <digest>` line does not match the kernel sources of this
+    tree (the capture predates a kernel change)."""
     import re
 
     p = ROOT / "profiles" / (summary or f"{kernel}_canonical.md")
     try:
-        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
-        return float(m.group(1)) if m else None
+        text = p.read_text()
     except OSError:
         return None
+    src = re.search(r"kernel_sources:\s*([0-9a-f]+)", text)
+    if not src or src.group(1) != kernel_source_digest():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", text)
+    return float(m.group(1)) if m else None
 
 
 def measured_peak_gbs() -> tuple[float, str]:

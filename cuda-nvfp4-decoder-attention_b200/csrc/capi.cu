@@ -1184,10 +1184,6 @@ int run_step(const nvfp4da_forward_args* a, const StepPlan& pl, void* ws, cudaSt
   p.tag_words = kStepTagWords;
   p.sync = slot;
   p.timeout_ns = 500ull * 1000 * 1000;
-  p.sched = 1;
-#ifdef NVFP4DA_PHASES
-  if (const char* v = std::getenv("NVFP4DA_STEP_SCHED")) p.sched = std::atoi(v);
-#endif
   p.off_qs = pl.off_qs;
   p.off_qw = pl.off_qw;
   p.off_kv = pl.off_kv;

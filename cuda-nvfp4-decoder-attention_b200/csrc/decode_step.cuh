@@ -93,8 +93,6 @@ struct StepParams {
   size_t tag_words;             // the region's size, cleared when the epoch wraps
   unsigned* sync;    // slot
   unsigned long long timeout_ns;
-  // Diagnostic build only: when the K/V tile and the O rows are requested.
-  int sched;
   // dynamic shared-memory layout (byte offsets); qs/qw/kv/q and comb overlay
   uint32_t off_qs, off_qw, off_kv, off_q, off_os, off_ow, off_xs, off_x16, off_red;
   // O rows decoded ahead into f16 rows at off_od (stride od_ld halves), which
@@ -330,15 +328,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
   [[maybe_unused]] constexpr unsigned kPhaseBase = 3072;
   constexpr int PPL = EPL / 2;  // RoPE pairs per lane (D = 32 * EPL)
   NVFP4DA_PHASE(0);
-#ifdef NVFP4DA_PHASES
-  if (p.sched & 32) {  // diagnostic: touch every line of the parameter block at once
-    constexpr int kLines = (sizeof(StepParams) + 127) / 128;
-    if (threadIdx.x < kLines) {
-      const uint32_t v = reinterpret_cast<const uint32_t*>(&p)[threadIdx.x * 32];
-      asm volatile("" ::"r"(v));
-    }
-  }
-#endif
 
   const int cta = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -451,18 +440,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
   // ---- input slices of this CTA (none is written by the step): the QKV
   // rows now, the K/V tile and the O rows once the QKV rows have landed, so
-  // that they do not queue ahead of the critical path.  (The diagnostic
-  // build, -DNVFP4DA_PHASES, can request them at other times through
-  // p.sched & 7: 0 both at launch; 2 the K/V tile then, the O rows after the
-  // attention unit; 3 the K/V tile at launch, the O rows once the QKV rows
-  // have landed; 4 the K/V tile at launch, the O rows as in 2.)
-#ifdef NVFP4DA_PHASES
-  const int sched = p.sched & 7;
-#else
-  constexpr int sched = 1;
-#endif
-  const bool kv_at_launch = sched == 0 || sched == 3 || sched == 4;
-  const int o_when = sched == 0 ? 0 : (sched == 2 || sched == 4 ? 2 : 1);
+  // that they do not queue ahead of the critical path (CTAs without QKV
+  // rows request them at once).
   auto issue_kv = [&]() {
     if (n_cache > 0) {
       const uint32_t tb = static_cast<uint32_t>(n_cache * d * 2);
@@ -479,9 +458,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
       bulk_g2s(ow_smem, p.packed[3] + orow0 * kb, wb, &bar_o);
     }
   };
-  if (threadIdx.x == 0) {
-    if (kv_at_launch || !has_qkv) issue_kv();
-    if (o_when == 0 || !has_qkv) issue_o();
+  if (threadIdx.x == 0 && !has_qkv) {
+    issue_kv();
+    issue_o();
   }
   NVFP4DA_PHASE(1);
   // Small inputs read late on the critical path (the projections' global
@@ -524,19 +503,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     NVFP4DA_PHASE(2);
     mbar_spin_until(&bar_qkv, 0, deadline, err);
     if (threadIdx.x == 0) {
-      if (!kv_at_launch) issue_kv();
-      if (o_when == 1 || (o_when == 2 && !has_attn)) issue_o();
+      issue_kv();
+      issue_o();
     }
     NVFP4DA_PHASE(3);
-#ifdef NVFP4DA_PHASES
-    if (p.sched & 16) {  // diagnostic: one step per loop iteration (small loop body)
-      if (f16)
-        mma_gemv_pass_smem<true, 1>(qw_smem, qs_smem, reinterpret_cast<const uint16_t*>(x16), k, p.rq, p.rq, mrows,
-                                    mred, outv);
-      else
-        mma_gemv_pass_smem<false, 1>(qw_smem, qs_smem, x_stage, k, p.rq, p.rq, mrows, mred, outv);
-    } else
-#endif
     if (f16)
       mma_gemv_pass_smem<true, 4>(qw_smem, qs_smem, reinterpret_cast<const uint16_t*>(x16), k, p.rq, p.rq, mrows,
                                   mred, outv);
@@ -848,7 +818,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         st_tagged(p.ctx + (b * k + (kvh * GH + g) * d + e) / 2, pair, tag);
       }
     }
-    if (threadIdx.x == 0 && o_when == 2 && has_qkv) issue_o();
     NVFP4DA_PHASE(9);
   }
 

@@ -261,7 +261,9 @@ int nvfp4da_attention_combine(const float* partials, int shards, int64_t rows, i
  * (cudaGetSymbolAddress) with the device current; make that first call before
  * any stream capture.  Allocates nothing.  All calls share the one array and
  * it keeps the last call's contents, so calls that overlap on the GPU (other
- * streams, other host threads) race and must be serialised by the caller. */
+ * streams, other host threads) race and must be serialised by the caller.
+ * The looked-up address is kept for the life of the process: resetting a
+ * device (cudaDeviceReset) after its first call is not supported. */
 #define NVFP4DA_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 int nvfp4da_decoder_attention_forward_noalloc(const nvfp4da_forward_args* args, void* stream);
 
