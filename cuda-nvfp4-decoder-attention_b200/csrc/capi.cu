@@ -21,6 +21,7 @@
 #include "attention_prefill.cuh"
 #include "attention_prefill_tc.cuh"
 #include "elementwise.cuh"
+#include "gemv_batched.cuh"
 #include "gemv_kernel.cuh"
 #include "prefill_gemm.cuh"
 #include "decode_step.cuh"
@@ -254,7 +255,34 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStream_t s,
   return cudaErrorInvalidConfiguration;
 }
 
+// ---------------------------------------------------------------- batched decode projections (8 < M <= 64)
+int bat_tiles(int64_t m) { return m <= 16 ? 2 : (m <= 32 ? 4 : 8); }
+
+template <int NT>
+cudaError_t launch_o_batched_t(const GemvParams& p, cudaStream_t s, bool pdl) {
+  auto* k = o_batched_kernel<NT>;
+  const uint32_t smem = bat_smem_bytes(p.k, NT * 8);
+  cudaError_t e = ensure_smem(k, smem);
+  if (e != cudaSuccess) return e;
+  return launch(k, dim3(static_cast<unsigned>(p.n / kBatRows)), dim3(kBatThreads), smem, s, pdl, p);
+}
+
+bool bat_linear_ok(const uint16_t* x, int64_t m, const nvfp4da_weight& w) {
+  return bat_shape_ok(m, w.rows, w.cols) && aligned(x, 16) && aligned(w.packed_values, 16) &&
+         aligned(w.block_scales, 16) && bat_smem_bytes(w.cols, 64) <= kMaxDynSmem &&
+         w.rows / kBatRows <= std::numeric_limits<int32_t>::max();
+}
+
 int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s, bool pdl) {
+  if (bat_linear_ok(x, m, w)) {
+    GemvParams p{x, m, w.packed_values, w.block_scales, w.global_decode_scale, y, w.rows, w.cols, nullptr, pdl ? 1 : 0};
+    const int nt = bat_tiles(m);
+    cudaError_t e = nt == 2 ? launch_o_batched_t<2>(p, s, pdl)
+                    : nt == 4 ? launch_o_batched_t<4>(p, s, pdl)
+                              : launch_o_batched_t<8>(p, s, pdl);
+    if (e != cudaSuccess) return cuda_fail(e, "batched w4a16 launch");
+    return NVFP4DA_OK;
+  }
   if (m >= kGemmMinMDecl && gemm_tc_supported(x, m, w, y)) return run_gemm_tc(x, m, w, y, s);
   GemvPlan pl;
   if (!plan_gemv(m, w.rows, w.cols, pl))
@@ -660,15 +688,38 @@ cudaError_t launch_qkv(const QkvParams& p, const QkvPlan& pl, int64_t units, cud
   }
 }
 
+template <int NT>
+cudaError_t launch_qkv_batched_t(const QkvParams& p, int64_t units, cudaStream_t s) {
+  auto* k = qkv_batched_kernel<NT>;
+  const uint32_t smem = bat_smem_bytes(p.hidden, NT * 8);
+  cudaError_t e = ensure_smem(k, smem);
+  if (e != cudaSuccess) return e;
+  return launch(k, dim3(static_cast<unsigned>(units * kQkvCluster)), dim3(kBatThreads), smem, s, true, p);
+}
+
+// The batched front half: the rows' RMSNorm and RoPE table, then the
+// projections with the head epilogue; both PDL-chained.
+cudaError_t launch_qkv_batched(const QkvParams& p, int64_t units, cudaStream_t s) {
+  cudaError_t e = launch(bat_norm_kernel, dim3(static_cast<unsigned>(p.m)), dim3(kNormThreads), 0, s, true, p);
+  if (e != cudaSuccess) return e;
+  const int nt = bat_tiles(p.m);
+  return nt == 2 ? launch_qkv_batched_t<2>(p, units, s)
+         : nt == 4 ? launch_qkv_batched_t<4>(p, units, s)
+                   : launch_qkv_batched_t<8>(p, units, s);
+}
+
 // ---------------------------------------------------------------- forward plan
 struct ForwardLayout {
   bool fused;
+  bool batched;  // fused path with the batched front half (bat_norm + qkv_batched)
   QkvPlan qkv;
   AttnPlan attn;
   size_t q_buf, ctx_buf, attn_ws, scratch;  // byte offsets
   size_t total;
   // modular-path buffers (offsets)
   size_t xn, qp, kp, vp, qn, kn, kr;
+  // batched front half (offsets)
+  size_t bxn, brope;
 };
 
 int check_forward(const nvfp4da_forward_args* a) {
@@ -710,6 +761,12 @@ int check_forward(const nvfp4da_forward_args* a) {
   return NVFP4DA_OK;
 }
 
+bool bat_weights_aligned(const nvfp4da_forward_args* a) {
+  for (const nvfp4da_weight* w : {&a->q_weight, &a->k_weight, &a->v_weight})
+    if (!aligned(w->packed_values, 16) || !aligned(w->block_scales, 16)) return false;
+  return true;
+}
+
 int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens;
   const int64_t maxp = a->past_lengths ? a->max_past_length : a->past_length;
@@ -719,6 +776,10 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   // tensor-core GEMM; the fused front half re-decodes its weights for every 8
   // activation rows.
   L.fused = m < kPrefillMinM && plan_qkv(m, a->hidden, a->head_dim, L.qkv);
+  L.batched = L.fused && a->head_dim == 4 * kBatRows && bat_shape_ok(m, a->hidden, a->hidden) &&
+              bat_smem_bytes(a->hidden, 64) <= kMaxDynSmem && aligned(a->x, 16) && aligned(a->input_norm_weight, 16) &&
+              !(a->stages && a->stages->input_normalized && !aligned(a->stages->input_normalized, 16)) &&
+              bat_weights_aligned(a);
   const size_t act = align_up(static_cast<size_t>(m * a->hidden) * 2, 256);
   const size_t kvact = align_up(static_cast<size_t>(m * a->kv_heads * a->head_dim) * 2, 256);
   size_t off = 0;
@@ -729,6 +790,12 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   L.attn_ws = off;
   off += L.attn.partial_bytes + L.attn.counter_bytes;
   L.scratch = off;
+  if (L.batched) {
+    L.bxn = off;
+    off += act;
+    L.brope = off;
+    off += align_up(static_cast<size_t>(m * (a->head_dim / 2)) * sizeof(float2), 256);
+  }
   if (!L.fused) {
     L.xn = off;
     off += act;
@@ -1466,7 +1533,14 @@ int forward_impl(const nvfp4da_forward_args* a, void* ws, size_t ws_bytes, void*
     p.zero_words = L.attn.counter_bytes ? reinterpret_cast<unsigned*>(static_cast<char*>(attn_ws) + L.attn.partial_bytes)
                                         : nullptr;
     p.n_zero_words = static_cast<int64_t>(L.attn.counter_bytes / 4);
-    cudaError_t e = launch_qkv(p, L.qkv, hq + 2 * a->kv_heads, s, true);
+    cudaError_t e;
+    if (L.batched) {
+      p.xn = reinterpret_cast<uint16_t*>(base + L.bxn);
+      p.rope_tab = reinterpret_cast<float2*>(base + L.brope);
+      e = launch_qkv_batched(p, hq + 2 * a->kv_heads, s);
+    } else {
+      e = launch_qkv(p, L.qkv, hq + 2 * a->kv_heads, s, true);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "fused qkv launch");
     r = run_attention(q_buf, a->k_cache, a->v_cache, ctx_buf, a->batch, a->tokens, hq, a->kv_heads, a->capacity, d,
                       a->past_length, a->past_lengths, maxp, attn_ws, L.attn.partial_bytes + L.attn.counter_bytes, s,

@@ -65,6 +65,11 @@ struct QkvParams {
   float2 rope_host[kMaxRopeRows][kMaxHeadDim / 2];
   // theta^(2m/D) rounded to FP32, from the host, for positions read on the device.
   float rope_denom[kMaxHeadDim / 2];
+  // Batched front half (gemv_batched.cuh): the normalised activation rows
+  // [M, H] and the RoPE (cos, sin) of every row [M, D/2], written by
+  // bat_norm_kernel and read by qkv_batched_kernel.
+  uint16_t* xn;
+  float2* rope_tab;
 };
 
 // Dynamic shared memory of the fused kernel: the MMA-GEMV layout followed by

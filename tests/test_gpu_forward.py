@@ -162,6 +162,9 @@ def small_case(b, t, h, hkv, d, p, c, seed):
     (1, 1, 96, 1, 48, 5, 9),      # D not a multiple of 32
     (3, 1, 256, 2, 64, 40, 64),   # fused path, D = 64
     (1, 2, 512, 1, 256, 9, 16),   # fused path, D = 256
+    (12, 1, 3072, 6, 128, 100, 128),  # batched front half and O projection, 12 rows (two n-tiles)
+    (2, 12, 1024, 2, 128, 7, 32),     # batched, T = 12: 24 rows at 12 positions per sequence
+    (40, 1, 512, 1, 128, 33, 40),     # batched, 40 rows (eight n-tiles, the last partly empty)
 ])
 def test_forward_general_shapes_match_oracle(b, t, h, hkv, d, p, c):
     inp, host_w = small_case(b, t, h, hkv, d, p, c, seed=b * 100 + t * 10 + d)

@@ -104,6 +104,22 @@ def test_w4a16_projection_sweep_matches_oracle(capi, m, n, k):
     assert m_.exact_fraction > 0.95, str(m_)
 
 
+@pytest.mark.parametrize("m,n,k", [(9, 4608, 3072), (24, 768, 3072), (33, 3072, 3072), (64, 3072, 3072),
+                                   (64, 4608, 512)])
+def test_w4a16_batched_rows_match_oracle(capi, m, n, k):
+    """8 < M <= 64 (the batched kernel: each weight fragment decoded once for
+    all rows), including row counts that leave part of the last n-tile empty."""
+    gen = torch.Generator().manual_seed(2000 + m + n + k)
+    x = torch.randn((m, k), generator=gen).to(torch.bfloat16)
+    s = oracle.quantize((0.02 * torch.randn((n, k), generator=gen)).numpy())
+    xb = host_bits(x)
+    y = capi.w4a16_linear(x.cuda(), dev_weight(s))
+    again = capi.w4a16_linear(x.cuda(), dev_weight(s))
+    assert torch.equal(y.view(torch.int16), again.view(torch.int16))  # deterministic
+    m_ = assert_stage_policy(host_bits(y), oracle.w4a16_linear(xb, s))
+    assert m_.exact_fraction > 0.95, str(m_)
+
+
 def test_w4a16_one_hot_weights_are_exact(capi):
     """Code 0x2 (1.0) at one input per output row, scale 0x38 (1.0), gamma 1:
     y[m, n] == x[m, (n + 3) % K] bit-for-bit (orientation and nibble order)."""
