@@ -256,7 +256,7 @@ cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStream_t s,
 }
 
 // ---------------------------------------------------------------- batched decode projections (8 < M <= 64)
-int bat_tiles(int64_t m) { return m <= 16 ? 2 : (m <= 32 ? 4 : 8); }
+int bat_tiles(int64_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : (m <= 32 ? 4 : 8)); }
 
 template <int NT>
 cudaError_t launch_o_batched_t(const GemvParams& p, cudaStream_t s, bool pdl) {
@@ -264,7 +264,7 @@ cudaError_t launch_o_batched_t(const GemvParams& p, cudaStream_t s, bool pdl) {
   const uint32_t smem = bat_smem_bytes(p.k, NT * 8);
   cudaError_t e = ensure_smem(k, smem);
   if (e != cudaSuccess) return e;
-  return launch(k, dim3(static_cast<unsigned>(p.n / kBatRows)), dim3(kBatThreads), smem, s, pdl, p);
+  return launch(k, dim3(static_cast<unsigned>(p.n / kBatRows * kBatCluster)), dim3(kBatThreads), smem, s, pdl, p);
 }
 
 bool bat_linear_ok(const uint16_t* x, int64_t m, const nvfp4da_weight& w) {
@@ -274,10 +274,13 @@ bool bat_linear_ok(const uint16_t* x, int64_t m, const nvfp4da_weight& w) {
 }
 
 int run_gemv(const uint16_t* x, int64_t m, const nvfp4da_weight& w, uint16_t* y, cudaStream_t s, bool pdl) {
-  if (bat_linear_ok(x, m, w)) {
+  // Up to 8 rows the decode GEMV (one pass, 192 CTAs of 16 rows) measured
+  // faster than the batched kernel (96 CTAs); from 9 rows it re-decodes.
+  if (m > kMmaMaxM && bat_linear_ok(x, m, w)) {
     GemvParams p{x, m, w.packed_values, w.block_scales, w.global_decode_scale, y, w.rows, w.cols, nullptr, pdl ? 1 : 0};
     const int nt = bat_tiles(m);
-    cudaError_t e = nt == 2 ? launch_o_batched_t<2>(p, s, pdl)
+    cudaError_t e = nt == 1 ? launch_o_batched_t<1>(p, s, pdl)
+                    : nt == 2 ? launch_o_batched_t<2>(p, s, pdl)
                     : nt == 4 ? launch_o_batched_t<4>(p, s, pdl)
                               : launch_o_batched_t<8>(p, s, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "batched w4a16 launch");
@@ -694,7 +697,7 @@ cudaError_t launch_qkv_batched_t(const QkvParams& p, int64_t units, cudaStream_t
   const uint32_t smem = bat_smem_bytes(p.hidden, NT * 8);
   cudaError_t e = ensure_smem(k, smem);
   if (e != cudaSuccess) return e;
-  return launch(k, dim3(static_cast<unsigned>(units * kQkvCluster)), dim3(kBatThreads), smem, s, true, p);
+  return launch(k, dim3(static_cast<unsigned>(units * kBatCluster)), dim3(kBatThreads), smem, s, true, p);
 }
 
 // The batched front half: the rows' RMSNorm and RoPE table, then the
@@ -703,7 +706,8 @@ cudaError_t launch_qkv_batched(const QkvParams& p, int64_t units, cudaStream_t s
   cudaError_t e = launch(bat_norm_kernel, dim3(static_cast<unsigned>(p.m)), dim3(kNormThreads), 0, s, true, p);
   if (e != cudaSuccess) return e;
   const int nt = bat_tiles(p.m);
-  return nt == 2 ? launch_qkv_batched_t<2>(p, units, s)
+  return nt == 1 ? launch_qkv_batched_t<1>(p, units, s)
+         : nt == 2 ? launch_qkv_batched_t<2>(p, units, s)
          : nt == 4 ? launch_qkv_batched_t<4>(p, units, s)
                    : launch_qkv_batched_t<8>(p, units, s);
 }
@@ -767,6 +771,8 @@ bool bat_weights_aligned(const nvfp4da_forward_args* a) {
   return true;
 }
 
+bool step_covers(const nvfp4da_forward_args* a);  // the one-kernel step plans this shape (below)
+
 int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens;
   const int64_t maxp = a->past_lengths ? a->max_past_length : a->past_length;
@@ -776,7 +782,12 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   // tensor-core GEMM; the fused front half re-decodes its weights for every 8
   // activation rows.
   L.fused = m < kPrefillMinM && plan_qkv(m, a->hidden, a->head_dim, L.qkv);
-  L.batched = L.fused && a->head_dim == 4 * kBatRows && bat_shape_ok(m, a->hidden, a->hidden) &&
+  // Up to 8 rows the batched front half only where the one-kernel step does
+  // not cover the shape: the step reproduces the decode kernels' Q/K/V sums
+  // bit for bit, so on its shapes the chain keeps those kernels.
+  L.batched = L.fused && a->head_dim == kBatRows && bat_shape_ok(m, a->hidden, a->hidden) &&
+              (m > kMmaMaxM || !step_covers(a)) &&
+              a->hidden <= 64 * kNormThreads &&
               bat_smem_bytes(a->hidden, 64) <= kMaxDynSmem && aligned(a->x, 16) && aligned(a->input_norm_weight, 16) &&
               !(a->stages && a->stages->input_normalized && !aligned(a->stages->input_normalized, 16)) &&
               bat_weights_aligned(a);
@@ -1193,6 +1204,11 @@ bool plan_step(const nvfp4da_forward_args* a, StepPlan& s) {
   s.xin = w + static_cast<size_t>(nb * k / 2) <= kStepTagWords ? w : StepPlan::kNoWords;
   s.total = 256;  // the step keeps nothing in the caller's workspace
   return true;
+}
+
+bool step_covers(const nvfp4da_forward_args* a) {
+  StepPlan sp;
+  return plan_step(a, sp);
 }
 
 // Whether the step can carry the activation rows of `a` in its parameter block.

@@ -1,4 +1,4 @@
-// Batched decode projections: W4A16 with 8 < M <= 64 activation rows.
+// Batched decode projections: W4A16 with 2 <= M <= 64 activation rows.
 //
 // Same semantics as the decode GEMV (reference/w4a16.py:11-59,
 // src/w4a16.cu:79-151): y[m, n] = BF16(gamma * sum_k x[m, k] * (q * beta)[n, k]),
@@ -9,31 +9,32 @@
 // n = 8 side of mma.m16n8k16 and walks the weights once per 8 rows, so at
 // M = 64 every CTA re-streams and re-decodes its weight slice eight times and
 // redoes the row preparation each time.  Here a weight fragment is decoded
-// once and multiplied into all M rows (NT = ceil(M / 8) n-tiles of 8 rows):
-//  * a CTA owns 32 weight rows (two 16-row tiles) over the whole K; its
-//    packed rows and scale rows (contiguous in the portable layout) are
-//    bulk-copied into shared memory at launch, before the programmatic-
-//    dependency wait;
-//  * the activation rows stream through a shared-memory ring (2-4 stages)
-//    in chunks of 512 k (one bulk copy per row and chunk, row stride 1,056
-//    bytes so the 16-byte operand loads of a warp hit distinct banks);
-//  * warp w takes the 128-k step w % 4 of every chunk and half of the
-//    n-tiles (w / 4): per chunk it decodes its 32 x 128 weight block
-//    (hardware E2M1/UE4M3 conversions) and issues 8 * NT BF16 MMAs; each
-//    activation operand is read from shared memory once per CTA;
-//  * the four step-warps are summed in a fixed order, so results are
-//    deterministic.
+// once and multiplied into all M rows (NT n-tiles of 8 rows):
+//  * a 4-CTA cluster owns 128 weight rows; CTA q of the cluster takes the
+//    K-quarter q of them, so each CTA reads only a quarter of the activation
+//    rows (every CTA reading whole rows made the activations' L2 lines the
+//    bottleneck: 144 CTAs x 384 KB at M = 64);
+//  * at launch, before the programmatic-dependency wait, the CTA bulk-copies
+//    its 128 x K/4 weight block and its scale block into shared memory; after
+//    the wait, its K-quarter of every activation row (row stride K/2 + 32
+//    bytes, so the 16-byte operand loads of a warp hit distinct banks);
+//  * warp w takes tiles 2 (w % 4) and 2 (w % 4) + 1 (32 weight rows) and the
+//    128-k steps s = w / 4 (mod 2) of the quarter: per step it decodes its
+//    weight block once (hardware E2M1/UE4M3 conversions) and issues
+//    4 * 2 * NT BF16 MMAs;
+//  * the two step-halves are summed in the CTA, then the four K-quarters
+//    through distributed shared memory, always in the same order, so results
+//    are deterministic.  CTA q finishes rows [32 q, 32 q + 32) of the block.
 // The k-permutation: lane (g, t) holds 16 contiguous weight bytes (k = 128 s
 // + 32 t .. + 31), word p of them (8 k) feeding MMA pair p.  Lanes with
 // t >= 2 take their words in the order 1, 0, 3, 2 (A and B alike), which
 // moves their operand loads to other shared-memory banks; every physical k
 // still meets the same activation k exactly once.
 //
-// The fused front half (qkv_batched_kernel) keeps the decode chain's stage
-// order -- input RMSNorm (bat_norm_kernel, once per row instead of once per
-// CTA), Q/K/V projection, per-head RMSNorm, RoPE, cache append -- with one
-// 4-CTA cluster per head as in qkv_fused_kernel; the O projection
-// (o_batched_kernel) writes BF16 rows.
+// The fused front half (qkv_batched_kernel, one cluster per head of D = 128)
+// keeps the decode chain's stage order -- input RMSNorm (bat_norm_kernel,
+// once per row), Q/K/V projection, per-head RMSNorm, RoPE, cache append; the
+// O projection (o_batched_kernel) writes BF16 rows.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -45,136 +46,127 @@
 
 namespace nvfp4da {
 
-constexpr int kBatMinM = 9;           // below this the decode GEMV is the better kernel
+constexpr int kBatMinM = 2;           // one row: the decode GEMV (latency-bound, no row reuse)
 constexpr int kBatMaxM = 64;
-constexpr int kBatRows = 32;          // weight rows per CTA
-constexpr int kBatChunkK = 512;       // k per activation chunk (4 steps of 128)
-constexpr int kBatRowStride = kBatChunkK * 2 + 32;  // bytes per activation row in a ring stage
+constexpr int kBatCluster = 4;        // K-quarters
+constexpr int kBatRows = 128;         // weight rows per cluster
+constexpr int kBatRowsPerCta = kBatRows / kBatCluster;
 constexpr int kBatThreads = 256;
 
-__host__ __device__ inline uint32_t bat_stage_bytes(int mpad) {
-  return static_cast<uint32_t>(mpad) * kBatRowStride;
+// Dynamic shared memory of one CTA (K-quarter kq = K / 4): scales [128][kq/16],
+// weights [128][kq/2], the activation rows [MP][kq * 2 + 32 bytes] (which the
+// step-half partials [128][MP] FP32 and then the CTA's results [32][MP]
+// overlay once the MMAs are done), and the inbox [4 quarters][32][MP] FP32
+// that the cluster's CTAs write their partials of this CTA's rows into.
+__host__ __device__ inline int64_t bat_quarter(int64_t k) { return k / kBatCluster; }
+__host__ __device__ inline uint32_t bat_row_stride(int64_t k) { return static_cast<uint32_t>(bat_quarter(k) * 2 + 32); }
+__host__ __device__ inline uint32_t bat_scale_bytes(int64_t k) { return static_cast<uint32_t>(kBatRows * (bat_quarter(k) / 16)); }
+__host__ __device__ inline uint32_t bat_weight_bytes(int64_t k) { return static_cast<uint32_t>(kBatRows * (bat_quarter(k) / 2)); }
+__host__ __device__ inline uint32_t bat_act_off(int64_t k) { return bat_scale_bytes(k) + bat_weight_bytes(k); }
+__host__ __device__ inline uint32_t bat_act_bytes(int64_t k, int mpad) {
+  const uint32_t rows = static_cast<uint32_t>(mpad) * bat_row_stride(k);
+  const uint32_t red = kBatRows * static_cast<uint32_t>(mpad) * 4u;
+  return rows > red ? rows : red;
 }
-// Ring stages: as many as fit beside the staged weights (a chunk of 64 rows
-// takes 66 KB).
-__host__ __device__ constexpr int bat_stages(int mpad) { return mpad >= 64 ? 2 : (mpad >= 32 ? 3 : 4); }
-// Dynamic shared memory: scales [32][K/16], packed weights [32][K/2], then
-// two ring stages.
-__host__ __device__ inline uint32_t bat_scale_bytes(int64_t k) { return r16(static_cast<uint64_t>(kBatRows) * (k / 16)); }
-__host__ __device__ inline uint32_t bat_weight_bytes(int64_t k) { return r16(static_cast<uint64_t>(kBatRows) * (k / 2)); }
-__host__ __device__ inline uint32_t bat_ring_off(int64_t k) { return bat_scale_bytes(k) + bat_weight_bytes(k); }
+__host__ __device__ inline uint32_t bat_inbox_bytes(int mpad) {
+  return static_cast<uint32_t>(kBatCluster * kBatRowsPerCta * mpad * 4);
+}
 __host__ __device__ inline uint32_t bat_smem_bytes(int64_t k, int mpad) {
-  return bat_ring_off(k) + bat_stages(mpad) * bat_stage_bytes(mpad);
+  return bat_act_off(k) + bat_act_bytes(k, mpad) + bat_inbox_bytes(mpad);
 }
-
-// Thread 0: bulk-copy the CTA's scale and packed rows (completion on `bar`).
-__device__ __forceinline__ void bat_stage_weights(uint8_t* smem, const uint8_t* scales, const uint8_t* packed,
-                                                  int64_t row0, int64_t k, uint64_t* bar) {
-  const uint32_t sbytes = static_cast<uint32_t>(kBatRows * (k / 16));
-  const uint32_t wbytes = static_cast<uint32_t>(kBatRows * (k / 2));
-  mbar_arrive_expect_tx(bar, sbytes + wbytes);
-  bulk_g2s(smem, scales + row0 * (k / 16), sbytes, bar);
-  bulk_g2s(smem + bat_scale_bytes(k), packed + row0 * (k / 2), wbytes, bar);
-}
+// K a multiple of 1024: each quarter whole 128-k steps and 16-byte multiples
+// of scale bytes per row (bulk-copy sizes).
 __host__ __device__ inline bool bat_shape_ok(int64_t m, int64_t n, int64_t k) {
-  return m >= kBatMinM && m <= kBatMaxM && k >= kBatChunkK && k % kBatChunkK == 0 && n % kBatRows == 0;
+  return m >= kBatMinM && m <= kBatMaxM && k >= 1024 && k % 1024 == 0 && n % kBatRows == 0;
 }
 
-// Issue the bulk copies of activation chunk c (rows [0, m) of xrows [M][K])
-// into ring stage c % S (warp 0 calls; lane 0 posts the byte count first).
-__device__ __forceinline__ void bat_issue_chunk(const uint16_t* xrows, int64_t k, int m, int c, int S, uint8_t* ring,
-                                                uint32_t stage_bytes, uint64_t* full) {
+// Warp 0: bulk-copy the CTA's scale and weight blocks (rows row0 ..
+// row0 + 127, K-quarter q) with completion on `bar`.
+__device__ __forceinline__ void bat_stage_weights(uint8_t* smem, const uint8_t* scales, const uint8_t* packed,
+                                                  int64_t row0, int64_t k, int q, uint64_t* bar) {
   const int lane = threadIdx.x & 31;
-  const int st = c % S;
-  if (lane == 0) mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(m) * (kBatChunkK * 2));
+  const int64_t kq = bat_quarter(k);
+  const uint32_t sb = static_cast<uint32_t>(kq / 16), wb = static_cast<uint32_t>(kq / 2);
+  if (lane == 0) mbar_arrive_expect_tx(bar, kBatRows * (sb + wb));
   __syncwarp();
-  for (int r = lane; r < m; r += 32)
-    bulk_g2s(ring + st * stage_bytes + r * kBatRowStride, xrows + static_cast<int64_t>(r) * k + c * kBatChunkK,
-             kBatChunkK * 2, &full[st]);
-}
-
-// This lane's weight bytes of chunk c (rows g and g + 8 of its tile, step
-// 4 c + j) from the staged rows, words swapped pairwise for lanes t >= 2
-// (see the header).
-__device__ __forceinline__ void bat_load_weights(const uint8_t* w_smem, int64_t k, int tile, int j, int c,
-                                                 uint4& lo, uint4& hi) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int64_t kb = k / 2;
-  const int s = c * 4 + j;
-  const uint8_t* plo = w_smem + static_cast<int64_t>(tile * 16 + g) * kb + s * 64 + 16 * t;
-  lo = *reinterpret_cast<const uint4*>(plo);
-  hi = *reinterpret_cast<const uint4*>(plo + 8 * kb);
-  if (t & 2) {
-    lo = make_uint4(lo.y, lo.x, lo.w, lo.z);
-    hi = make_uint4(hi.y, hi.x, hi.w, hi.z);
+  for (int r = lane; r < kBatRows; r += 32) {
+    bulk_g2s(smem + r * sb, scales + (row0 + r) * (k / 16) + q * sb, sb, bar);
+    bulk_g2s(smem + bat_scale_bytes(k) + r * wb, packed + (row0 + r) * (k / 2) + q * wb, wb, bar);
   }
 }
 
-// The CTA's 32 rows x M outputs (before gamma) into out[r * MP + m], MP = 8 NT.
-// Called by all threads after the programmatic-dependency wait (xrows may be
-// an earlier kernel's output).  `smem` holds the staged scale and weight rows
-// (bat_stage_weights, completion on wbar) and the ring.  Bounded waits: a
-// timeout is recorded in *err (when given) and the pass carries on with
-// whatever the buffers hold.
+// Warp 0: bulk-copy K-quarter q of activation rows [0, m) (completion on `bar`).
+__device__ __forceinline__ void bat_stage_rows(uint8_t* dst, const uint16_t* xrows, int64_t k, int m, int q,
+                                               uint64_t* bar) {
+  const int lane = threadIdx.x & 31;
+  const int64_t kq = bat_quarter(k);
+  const uint32_t bytes = static_cast<uint32_t>(kq * 2);
+  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(m) * bytes);
+  __syncwarp();
+  for (int r = lane; r < m; r += 32)
+    bulk_g2s(dst + r * bat_row_stride(k), xrows + static_cast<int64_t>(r) * k + q * kq, bytes, bar);
+}
+
+// The cluster's 128 rows x M outputs: CTA q returns rows [32 q, 32 q + 32)
+// (before gamma) as [32][MP] FP32 in its own shared memory (the pointer
+// returned).  All threads of every CTA of the cluster call it after the
+// programmatic-dependency wait; the weight copies were issued on `wbar`
+// before it.  Bounded waits: a timeout is recorded in *err (when given) and
+// the pass carries on with whatever the buffers hold.  After it returns no
+// CTA touches another's shared memory.
 template <int NT, unsigned PHASE_BASE>
-__device__ __forceinline__ void bat_pass(uint8_t* smem, uint64_t* wbar, const uint16_t* xrows, int64_t k, int m,
-                                         uint64_t* full, unsigned* err, float* out) {
+__device__ __forceinline__ const float* bat_pass(uint8_t* smem, uint64_t* wbar, uint64_t* xbar, const uint16_t* xrows,
+                                                 int64_t k, int m, unsigned* err) {
   [[maybe_unused]] constexpr unsigned kPhaseBase = PHASE_BASE;
   constexpr int MP = NT * 8;
-  constexpr int S = bat_stages(MP);
-  constexpr int NH = NT / 2;  // n-tiles per warp
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int q = static_cast<int>(cluster.block_rank());
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
-  const int j = warp & 3, nh = warp >> 2;
-  const uint32_t sb = bat_stage_bytes(MP);
-  const int chunks = static_cast<int>(k / kBatChunkK);
-  const int64_t ks = k / 16;
+  const int tp = warp & 3, sh = warp >> 2;  // tile pair, step parity
+  const int64_t kq = bat_quarter(k);
+  const int steps = static_cast<int>(kq / 128);
+  const uint32_t ks = static_cast<uint32_t>(kq / 16), kb = static_cast<uint32_t>(kq / 2), rs = bat_row_stride(k);
   const uint8_t* s_smem = smem;
   const uint8_t* w_smem = smem + bat_scale_bytes(k);
-  uint8_t* ring = smem + bat_ring_off(k);
-  if (warp == 0)
-    for (int c = 0; c < S && c < chunks; ++c) bat_issue_chunk(xrows, k, m, c, S, ring, sb, full);
-  mbar_wait_bounded(wbar, 0, err);
-  NVFP4DA_PHASE(3);
-  uint4 w[2][2];  // [tile][lo / hi rows]
-#pragma unroll
-  for (int tl = 0; tl < 2; ++tl) bat_load_weights(w_smem, k, tl, j, 0, w[tl][0], w[tl][1]);
-  const uint8_t* sc0 = s_smem + g * ks + 2 * t;  // rows g, g + 8, g + 16, g + 24
-  // operand byte offset of (row g of n-tile nh * NH, step j, lane t) inside a
-  // stage; word p at + 16 (p ^ (t >> 1))
-  const uint32_t xoff = (nh * NH * 8 + g) * kBatRowStride + j * 256 + t * 64;
+  uint8_t* act = smem + bat_act_off(k);
+  if (warp == 0) bat_stage_rows(act, xrows, k, m, q, xbar);
+  // lane's bytes: rows 32 tp + g + 8 r (r = 0..3: tiles 2 tp, 2 tp + 1, lower / upper half)
+  const uint8_t* wl0 = w_smem + (32 * tp + g) * kb + 16 * t;
+  const uint8_t* sc0 = s_smem + (32 * tp + g) * ks + 2 * t;
+  // operand byte offset of (row g, lane t) in the staged rows; word p at + 16 (p ^ (t >> 1))
+  const uint8_t* xs0 = act + g * rs + t * 64;
   const uint32_t pswap = (t >> 1) & 1;
-  float d[2][NH][4];
+  float d[2][NT][4];
 #pragma unroll
   for (int tl = 0; tl < 2; ++tl)
 #pragma unroll
-    for (int n = 0; n < NH; ++n) d[tl][n][0] = d[tl][n][1] = d[tl][n][2] = d[tl][n][3] = 0.0f;
-  for (int c = 0; c < chunks; ++c) {
-    const int st = c % S;
-    uint4 wn[2][2];
-#pragma unroll
-    for (int tl = 0; tl < 2; ++tl) {
-      wn[tl][0] = w[tl][0];
-      wn[tl][1] = w[tl][1];
-      if (c + 1 < chunks) bat_load_weights(w_smem, k, tl, j, c + 1, wn[tl][0], wn[tl][1]);
-    }
-    const int s = c * 4 + j;
+    for (int n = 0; n < NT; ++n) d[tl][n][0] = d[tl][n][1] = d[tl][n][2] = d[tl][n][3] = 0.0f;
+  mbar_wait_bounded(wbar, 0, err);
+  NVFP4DA_PHASE(3);
+  mbar_wait_bounded(xbar, 0, err);
+  NVFP4DA_PHASE(4);
+  for (int s = sh; s < steps; s += 2) {
+    uint4 wv[4];
     uint32_t bs[4][2];  // block scales (f16x2) of rows g + 8 r, blocks 2 t and 2 t + 1 of step s
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
+      wv[r] = *reinterpret_cast<const uint4*>(wl0 + 8 * r * kb + s * 64);
+      if (t & 2) wv[r] = make_uint4(wv[r].y, wv[r].x, wv[r].w, wv[r].z);
       const uint32_t s2 = *reinterpret_cast<const uint16_t*>(sc0 + 8 * r * ks + 8 * s);
       bs[r][0] = ue4m3_to_f16x2_dup(s2);
       bs[r][1] = ue4m3_to_f16x2_dup(s2 >> 8);
     }
-    mbar_wait_bounded(&full[st], static_cast<uint32_t>(c / S) & 1u, err);
-    const uint8_t* xs = ring + st * sb + xoff;
+    const uint8_t* xs = xs0 + s * 256;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       // register word p is physical word p ^ pswap; its scale block is the same (p >> 1)
       uint32_t a[2][2][4];  // [tile][k half][fragment]
 #pragma unroll
       for (int tl = 0; tl < 2; ++tl) {
-        const uint32_t wl[4] = {w[tl][0].x, w[tl][0].y, w[tl][0].z, w[tl][0].w};
-        const uint32_t wh[4] = {w[tl][1].x, w[tl][1].y, w[tl][1].z, w[tl][1].w};
+        const uint4 lo = wv[2 * tl], hi = wv[2 * tl + 1];
+        const uint32_t wl[4] = {lo.x, lo.y, lo.z, lo.w};
+        const uint32_t wh[4] = {hi.x, hi.y, hi.z, hi.w};
         uint32_t q0[4], q1[4];
         e2m1x8_to_f16x2x4(wl[p], q0);
         e2m1x8_to_f16x2x4(wh[p], q1);
@@ -188,8 +180,8 @@ __device__ __forceinline__ void bat_pass(uint8_t* smem, uint64_t* wbar, const ui
       }
       const uint32_t wo = 16u * (static_cast<uint32_t>(p) ^ pswap);
 #pragma unroll
-      for (int n = 0; n < NH; ++n) {
-        const uint4 xb = *reinterpret_cast<const uint4*>(xs + n * 8 * kBatRowStride + wo);
+      for (int n = 0; n < NT; ++n) {
+        const uint4 xb = *reinterpret_cast<const uint4*>(xs + n * 8 * rs + wo);
 #pragma unroll
         for (int tl = 0; tl < 2; ++tl) {
           mma_bf16(d[tl][n], a[tl][0], xb.x, xb.y);
@@ -197,38 +189,51 @@ __device__ __forceinline__ void bat_pass(uint8_t* smem, uint64_t* wbar, const ui
         }
       }
     }
-#pragma unroll
-    for (int tl = 0; tl < 2; ++tl) {
-      w[tl][0] = wn[tl][0];
-      w[tl][1] = wn[tl][1];
-    }
-    __syncthreads();  // every warp is done with stage st
-    if (warp == 0 && c + S < chunks) bat_issue_chunk(xrows, k, m, c + S, S, ring, sb, full);
   }
-  NVFP4DA_PHASE(4);
-  // Sum the four step-warps in step order (stage 0 holds the partials: its
-  // last chunk has been consumed, and no copy is in flight).
-  float* red = reinterpret_cast<float*>(ring);  // [j][32 rows][MP]
-  float* rw = red + j * kBatRows * MP;
-#pragma unroll
-  for (int tl = 0; tl < 2; ++tl)
-#pragma unroll
-    for (int n = 0; n < NH; ++n) {
-      const int col = (nh * NH + n) * 8 + 2 * t, r0 = tl * 16 + g;
-      rw[r0 * MP + col] = d[tl][n][0];
-      rw[r0 * MP + col + 1] = d[tl][n][1];
-      rw[(r0 + 8) * MP + col] = d[tl][n][2];
-      rw[(r0 + 8) * MP + col + 1] = d[tl][n][3];
-    }
-  __syncthreads();
-  for (int i = threadIdx.x; i < kBatRows * MP; i += kBatThreads) {
-    float v = 0.0f;
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) v += red[jj * kBatRows * MP + i];
-    out[i] = v;
-  }
-  __syncthreads();
   NVFP4DA_PHASE(5);
+  __syncthreads();  // every warp is done with the activation rows
+  // Step-half 1 leaves its partials in shared memory; step-half 0 adds its
+  // own and writes the sums of rows [32 tp, 32 tp + 32) straight into the
+  // inbox of cluster CTA tp (slot q), which owns those rows.
+  float* half = reinterpret_cast<float*>(act);  // [128][MP]
+  if (sh == 1) {
+#pragma unroll
+    for (int tl = 0; tl < 2; ++tl)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        float* rw = half + (32 * tp + 16 * tl + g) * MP + n * 8 + 2 * t;
+        rw[0] = d[tl][n][0];
+        rw[1] = d[tl][n][1];
+        rw[8 * MP] = d[tl][n][2];
+        rw[8 * MP + 1] = d[tl][n][3];
+      }
+  }
+  __syncthreads();
+  float* inbox = reinterpret_cast<float*>(act + bat_act_bytes(k, MP));  // [4][32][MP]
+  if (sh == 0) {
+    float* dst = cluster.map_shared_rank(inbox, tp) + q * kBatRowsPerCta * MP;
+#pragma unroll
+    for (int tl = 0; tl < 2; ++tl)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int r = 16 * tl + g, col = n * 8 + 2 * t;
+        const float* hr = half + (32 * tp + r) * MP + col;
+        float* o = dst + r * MP + col;
+        *reinterpret_cast<float2*>(o) = make_float2(d[tl][n][0] + hr[0], d[tl][n][1] + hr[1]);
+        *reinterpret_cast<float2*>(o + 8 * MP) = make_float2(d[tl][n][2] + hr[8 * MP], d[tl][n][3] + hr[8 * MP + 1]);
+      }
+  }
+  cluster.sync();  // every quarter's partials of every CTA's rows have landed
+  NVFP4DA_PHASE(6);
+  // This CTA's rows: the four quarters in cluster-rank order.
+  float* out = reinterpret_cast<float*>(act);  // [32][MP] (the step-half partials are consumed)
+  for (int i = threadIdx.x; i < kBatRowsPerCta * MP; i += kBatThreads) {
+    const float* v = inbox + i;
+    out[i] = ((v[0] + v[kBatRowsPerCta * MP]) + v[2 * kBatRowsPerCta * MP]) + v[3 * kBatRowsPerCta * MP];
+  }
+  __syncthreads();
+  NVFP4DA_PHASE(7);
+  return out;
 }
 
 // ---------------------------------------------------------------- input RMSNorm + RoPE table
@@ -242,66 +247,27 @@ __global__ void __launch_bounds__(kNormThreads) bat_norm_kernel(const __grid_con
   [[maybe_unused]] constexpr unsigned kPhaseBase = 3584;
   NVFP4DA_PHASE(0);
   pdl_launch_dependents();  // the projection kernel may stage its weights meanwhile
+  const int64_t row = blockIdx.x, k = p.hidden;
+  // 16-byte chunks, up to kB per thread, all in flight at once (the gain
+  // never depends on an earlier kernel, so it is requested before the wait).
+  constexpr int kB = 8;  // K <= 8 * 8 * kNormThreads (checked by the host)
+  const int kv8 = static_cast<int>(k / 8);
+  const uint4* gr = reinterpret_cast<const uint4*>(p.g_in);
+  uint4 v[kB], gg[kB];
+#pragma unroll
+  for (int i = 0; i < kB; ++i) {
+    const int idx = threadIdx.x + i * kNormThreads;
+    gg[i] = idx < kv8 ? gr[idx] : make_uint4(0u, 0u, 0u, 0u);
+  }
   pdl_wait();
   NVFP4DA_PHASE(1);
-  const int64_t row = blockIdx.x, k = p.hidden;
-  // 16-byte chunks, eight per thread in flight (K % 512 == 0 here).
   const uint4* xr = reinterpret_cast<const uint4*>(p.x + row * k);
-  const uint4* gr = reinterpret_cast<const uint4*>(p.g_in);
-  const int kv8 = static_cast<int>(k / 8);
-  constexpr int kB = 8;
-  double ss = 0.0;
-  for (int base = threadIdx.x; base < kv8; base += kB * kNormThreads) {
-    uint4 v[kB];
 #pragma unroll
-    for (int i = 0; i < kB; ++i) {
-      const int idx = base + i * kNormThreads;
-      v[i] = idx < kv8 ? xr[idx] : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < kB; ++i) {
-      const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float a = __uint_as_float(wv[q] << 16), c = __uint_as_float(wv[q] & 0xffff0000u);
-        ss += static_cast<double>(a * a) + static_cast<double>(c * c);
-      }
-    }
+  for (int i = 0; i < kB; ++i) {
+    const int idx = threadIdx.x + i * kNormThreads;
+    v[i] = idx < kv8 ? xr[idx] : make_uint4(0u, 0u, 0u, 0u);
   }
-  NVFP4DA_PHASE(3);
-  const double tot = block_sum_f64(ss, scratch);
-  NVFP4DA_PHASE(4);
-  const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
-  NVFP4DA_PHASE(5);
-  uint4* xo = reinterpret_cast<uint4*>(p.xn + row * k);
-  uint4* dbg = p.dbg_xnorm ? reinterpret_cast<uint4*>(p.dbg_xnorm + row * k) : nullptr;
-  for (int base = threadIdx.x; base < kv8; base += kB * kNormThreads) {
-    uint4 v[kB], gg[kB];
-#pragma unroll
-    for (int i = 0; i < kB; ++i) {
-      const int idx = base + i * kNormThreads;
-      v[i] = idx < kv8 ? xr[idx] : make_uint4(0u, 0u, 0u, 0u);
-      gg[i] = idx < kv8 ? gr[idx] : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < kB; ++i) {
-      const int idx = base + i * kNormThreads;
-      if (idx >= kv8) break;
-      const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w}, wg[4] = {gg[i].x, gg[i].y, gg[i].z, gg[i].w};
-      uint32_t o[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float lo = __fmul_rn(__fmul_rn(__uint_as_float(wv[q] << 16), inv), __uint_as_float(wg[q] << 16));
-        const float hi =
-            __fmul_rn(__fmul_rn(__uint_as_float(wv[q] & 0xffff0000u), inv), __uint_as_float(wg[q] & 0xffff0000u));
-        o[q] = static_cast<uint32_t>(f32_to_bf16_bits(lo)) | (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
-      }
-      const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
-      xo[idx] = nv;
-      if (dbg) dbg[idx] = nv;
-    }
-  }
-  NVFP4DA_PHASE(6);
+  // The row's RoPE table while the loads are in flight.
   const int64_t b = row / p.tokens, t = row % p.tokens;
   const int64_t pos = (p.past_lengths ? p.past_lengths[b] : p.past_length) + t;
   const int64_t pairs = p.head_dim / 2;
@@ -315,17 +281,50 @@ __global__ void __launch_bounds__(kNormThreads) bat_norm_kernel(const __grid_con
     }
     p.rope_tab[row * pairs + pr] = make_float2(c, sn);
   }
+  NVFP4DA_PHASE(3);
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < kB; ++i) {
+    const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float a = __uint_as_float(wv[q] << 16), c = __uint_as_float(wv[q] & 0xffff0000u);
+      ss += static_cast<double>(a * a) + static_cast<double>(c * c);
+    }
+  }
+  const double tot = block_sum_f64(ss, scratch);
+  NVFP4DA_PHASE(4);
+  const float inv = rms_inverse(static_cast<float>(tot), static_cast<float>(k), p.eps);
+  uint4* xo = reinterpret_cast<uint4*>(p.xn + row * k);
+  uint4* dbg = p.dbg_xnorm ? reinterpret_cast<uint4*>(p.dbg_xnorm + row * k) : nullptr;
+#pragma unroll
+  for (int i = 0; i < kB; ++i) {
+    const int idx = threadIdx.x + i * kNormThreads;
+    if (idx >= kv8) break;
+    const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w}, wg[4] = {gg[i].x, gg[i].y, gg[i].z, gg[i].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = __fmul_rn(__fmul_rn(__uint_as_float(wv[q] << 16), inv), __uint_as_float(wg[q] << 16));
+      const float hi =
+          __fmul_rn(__fmul_rn(__uint_as_float(wv[q] & 0xffff0000u), inv), __uint_as_float(wg[q] & 0xffff0000u));
+      o[q] = static_cast<uint32_t>(f32_to_bf16_bits(lo)) | (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+    }
+    const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
+    xo[idx] = nv;
+    if (dbg) dbg[idx] = nv;
+  }
   NVFP4DA_PHASE(2);
 }
 
 // ---------------------------------------------------------------- fused front half, D = 128
 template <int NT>
-__global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kBatThreads, 1)
+__global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThreads, 1)
     qkv_batched_kernel(const __grid_constant__ QkvParams p) {
   constexpr int MP = NT * 8;
-  constexpr int D = 4 * kBatRows;  // one head per cluster
+  constexpr int D = kBatRows;  // one head per cluster
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t sbar, full[4];
+  __shared__ uint64_t wbar, xbar;
   __shared__ __align__(16) uint16_t head_out[MP][D];
   [[maybe_unused]] constexpr unsigned kPhaseBase = 0;
   NVFP4DA_PHASE(0);
@@ -334,7 +333,7 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kBatThread
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
-  const int64_t unit = blockIdx.x / kQkvCluster;
+  const int64_t unit = blockIdx.x / kBatCluster;
   const int64_t k = p.hidden;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int m = static_cast<int>(p.m);
@@ -350,33 +349,31 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kBatThread
     mat = 2;
     head = unit - p.q_heads - p.kv_heads;
   }
-  const int64_t row0 = head * D + static_cast<int64_t>(rank) * kBatRows;
-  float* outv = reinterpret_cast<float*>(smem + bat_ring_off(k) + bat_stage_bytes(MP));  // [32][MP], after the pass
+  const int64_t row0 = head * D;
 
   if (threadIdx.x == 0) {
-    mbar_init(&sbar, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&full[i], 1);
+    mbar_init(&wbar, 1);
+    mbar_init(&xbar, 1);
     fence_mbar_init();
-    bat_stage_weights(smem, p.scales[mat], p.packed[mat], row0, k, &sbar);
   }
-  const float gamma = *p.gamma[mat];
   __syncthreads();  // the barriers are initialised
+  if (warp == 0) bat_stage_weights(smem, p.scales[mat], p.packed[mat], row0, k, rank, &wbar);
+  const float gamma = *p.gamma[mat];
   NVFP4DA_PHASE(1);
 
   pdl_wait();
   NVFP4DA_PHASE(2);
   if (blockIdx.x == 0)
     for (int64_t i = threadIdx.x; i < p.n_zero_words; i += blockDim.x) p.zero_words[i] = 0u;
-  bat_pass<NT, 0>(smem, &sbar, p.xn, k, m, full, p.err, outv);
-  NVFP4DA_PHASE(6);
+  const float* outv = bat_pass<NT, 0>(smem, &wbar, &xbar, p.xn, k, m, p.err);
 
   uint16_t* leader_out = cluster.map_shared_rank(&head_out[0][0], 0);
-  for (int i = threadIdx.x; i < kBatRows * m; i += kBatThreads) {
-    const int n = i / kBatRows, r = i % kBatRows;
-    leader_out[n * D + rank * kBatRows + r] = f32_to_bf16_bits(__fmul_rn(outv[r * MP + n], gamma));
+  for (int i = threadIdx.x; i < kBatRowsPerCta * m; i += kBatThreads) {
+    const int n = i / kBatRowsPerCta, r = i % kBatRowsPerCta;
+    leader_out[n * D + rank * kBatRowsPerCta + r] = f32_to_bf16_bits(__fmul_rn(outv[r * MP + n], gamma));
   }
   cluster.sync();
-  NVFP4DA_PHASE(7);
+  NVFP4DA_PHASE(8);
   if (rank != 0) return;
 
   // ---- head epilogue (the leader): activation row mrow per warp
@@ -442,35 +439,37 @@ __global__ void __cluster_dims__(kQkvCluster, 1, 1) __launch_bounds__(kBatThread
 
 // ---------------------------------------------------------------- O projection (any W4A16 linear)
 template <int NT>
-__global__ void __launch_bounds__(kBatThreads, 1) o_batched_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThreads, 1)
+    o_batched_kernel(const __grid_constant__ GemvParams p) {
   constexpr int MP = NT * 8;
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t sbar, full[4];
+  __shared__ uint64_t wbar, xbar;
+  namespace cg = cooperative_groups;
+  const int rank = static_cast<int>(cg::this_cluster().block_rank());
   const int64_t k = p.k;
   const int m = static_cast<int>(p.m);
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kBatRows;
-  float* outv = reinterpret_cast<float*>(smem + bat_ring_off(k) + bat_stage_bytes(MP));
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x / kBatCluster) * kBatRows;
   [[maybe_unused]] constexpr unsigned kPhaseBase = 2048;
   NVFP4DA_PHASE(0);
   if (threadIdx.x == 0) {
-    mbar_init(&sbar, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(&full[i], 1);
+    mbar_init(&wbar, 1);
+    mbar_init(&xbar, 1);
     fence_mbar_init();
-    bat_stage_weights(smem, p.scales, p.packed, row0, k, &sbar);
   }
-  const float gamma = *p.gamma;
   __syncthreads();
+  if ((threadIdx.x >> 5) == 0) bat_stage_weights(smem, p.scales, p.packed, row0, k, rank, &wbar);
+  const float gamma = *p.gamma;
   NVFP4DA_PHASE(1);
   if (p.pdl) {
     pdl_wait();
     pdl_launch_dependents();
   }
   NVFP4DA_PHASE(2);
-  bat_pass<NT, 2048>(smem, &sbar, p.x, k, m, full, p.err, outv);
-  NVFP4DA_PHASE(6);
-  for (int i = threadIdx.x; i < kBatRows * m; i += kBatThreads) {
-    const int n = i / kBatRows, r = i % kBatRows;
-    p.y[n * p.n + row0 + r] = f32_to_bf16_bits(__fmul_rn(outv[r * MP + n], gamma));
+  const float* outv = bat_pass<NT, 2048>(smem, &wbar, &xbar, p.x, k, m, p.err);
+  const int64_t r0 = row0 + rank * kBatRowsPerCta;
+  for (int i = threadIdx.x; i < kBatRowsPerCta * m; i += kBatThreads) {
+    const int n = i / kBatRowsPerCta, r = i % kBatRowsPerCta;
+    p.y[n * p.n + r0 + r] = f32_to_bf16_bits(__fmul_rn(outv[r * MP + n], gamma));
   }
 }
 

@@ -105,7 +105,7 @@ def test_w4a16_projection_sweep_matches_oracle(capi, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(9, 4608, 3072), (24, 768, 3072), (33, 3072, 3072), (64, 3072, 3072),
-                                   (64, 4608, 512)])
+                                   (64, 4608, 1024), (17, 256, 2048)])
 def test_w4a16_batched_rows_match_oracle(capi, m, n, k):
     """8 < M <= 64 (the batched kernel: each weight fragment decoded once for
     all rows), including row counts that leave part of the last n-tile empty."""
