@@ -504,7 +504,8 @@ def run_c2_batch_sharded(capi, world, rank, stream, peak, steps=50) -> dict:
             "tokens_per_s": round(full.batch / (ms_step * 1e-3), 1), "ms_per_step": round(ms_step, 5),
             "hbm_gbs_per_gpu": round(gbs, 1), "frac_per_gpu": round(gbs / peak, 4),
             "bytes_per_step_job": int(tot.item()), "bytes_per_step_rank0": bytes_rank,
-            "path": "fused QKV + streaming split-KV attention + O GEMV (3 PDL-chained launches per rank)",
+            "path": ("input RMSNorm + batched QKV/head epilogue (4-CTA clusters, split K) + streaming split-KV "
+                     "attention + batched O projection (4 PDL-chained launches per rank)"),
             "replicas": n_rep, "graph": graphed, "steps": reps * n_rep}
 
 

@@ -773,6 +773,26 @@ bool bat_weights_aligned(const nvfp4da_forward_args* a) {
 
 bool step_covers(const nvfp4da_forward_args* a);  // the one-kernel step plans this shape (below)
 
+// The batched front half (bat_norm_kernel + qkv_batched_kernel) applies:
+// 2..64 rows, D = 128, K a multiple of 1024 that fits its shared memory and
+// the norm kernel's registers, 16-byte aligned rows, gains and weights.
+bool bat_front_ok(const nvfp4da_forward_args* a) {
+  const int64_t m = a->batch * a->tokens;
+  return a->head_dim == kBatRows && bat_shape_ok(m, a->hidden, a->hidden) && a->hidden <= 64 * kNormThreads &&
+         bat_smem_bytes(a->hidden, 64) <= kMaxDynSmem && aligned(a->x, 16) && aligned(a->input_norm_weight, 16) &&
+         !(a->stages && a->stages->input_normalized && !aligned(a->stages->input_normalized, 16)) &&
+         bat_weights_aligned(a);
+}
+
+// Its scratch: the normalised rows [M, H] BF16 (256-byte padded), then the
+// RoPE table [M, D/2].
+size_t bat_rows_bytes(const nvfp4da_forward_args* a) {
+  return align_up(static_cast<size_t>(a->batch * a->tokens * a->hidden) * 2, 256);
+}
+size_t bat_front_bytes(const nvfp4da_forward_args* a) {
+  return bat_rows_bytes(a) + align_up(static_cast<size_t>(a->batch * a->tokens * (a->head_dim / 2)) * sizeof(float2), 256);
+}
+
 int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   const int64_t hq = a->hidden / a->head_dim, m = a->batch * a->tokens;
   const int64_t maxp = a->past_lengths ? a->max_past_length : a->past_length;
@@ -785,12 +805,7 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   // Up to 8 rows the batched front half only where the one-kernel step does
   // not cover the shape: the step reproduces the decode kernels' Q/K/V sums
   // bit for bit, so on its shapes the chain keeps those kernels.
-  L.batched = L.fused && a->head_dim == kBatRows && bat_shape_ok(m, a->hidden, a->hidden) &&
-              (m > kMmaMaxM || !step_covers(a)) &&
-              a->hidden <= 64 * kNormThreads &&
-              bat_smem_bytes(a->hidden, 64) <= kMaxDynSmem && aligned(a->x, 16) && aligned(a->input_norm_weight, 16) &&
-              !(a->stages && a->stages->input_normalized && !aligned(a->stages->input_normalized, 16)) &&
-              bat_weights_aligned(a);
+  L.batched = L.fused && bat_front_ok(a) && (m > kMmaMaxM || !step_covers(a));
   const size_t act = align_up(static_cast<size_t>(m * a->hidden) * 2, 256);
   const size_t kvact = align_up(static_cast<size_t>(m * a->kv_heads * a->head_dim) * 2, 256);
   size_t off = 0;
@@ -803,9 +818,8 @@ int plan_forward(const nvfp4da_forward_args* a, ForwardLayout& L) {
   L.scratch = off;
   if (L.batched) {
     L.bxn = off;
-    off += act;
-    L.brope = off;
-    off += align_up(static_cast<size_t>(m * (a->head_dim / 2)) * sizeof(float2), 256);
+    L.brope = off + act;
+    off += bat_front_bytes(a);
   }
   if (!L.fused) {
     L.xn = off;
@@ -1642,8 +1656,13 @@ static int64_t shard_visible_max(int64_t max_past, int64_t tokens, int64_t shard
   return v < 1 ? 1 : v;
 }
 
+size_t nvfp4da_qkv_rope_append_shard_workspace_size(const nvfp4da_forward_args* a) {
+  if (!a || a->batch <= 0 || a->tokens <= 0 || a->hidden <= 0 || a->head_dim <= 0) return 0;
+  return bat_front_ok(a) ? bat_front_bytes(a) : 0;
+}
+
 int nvfp4da_qkv_rope_append_shard(const nvfp4da_forward_args* a, int64_t shard_start, int64_t global_capacity,
-                                  uint16_t* q_rope_out, void* stream) {
+                                  uint16_t* q_rope_out, void* ws, size_t ws_bytes, void* stream) {
   if (!a) return fail(NVFP4DA_ERR_INVALID_ARGUMENT, "args is NULL");
   if (shard_start < 0 || a->capacity <= 0 || global_capacity <= 0 ||
       shard_start > global_capacity - a->capacity)
@@ -1661,7 +1680,17 @@ int nvfp4da_qkv_rope_append_shard(const nvfp4da_forward_args* a, int64_t shard_s
   QkvParams p = qkv_params(a, q_rope_out);
   p.slot_offset = shard_start;
   const int64_t hq = a->hidden / a->head_dim;
-  cudaError_t e = launch_qkv(p, pl, hq + 2 * a->kv_heads, static_cast<cudaStream_t>(stream), true);
+  cudaError_t e;
+  if (ws && bat_front_ok(a)) {
+    if (ws_bytes < bat_front_bytes(a) || !aligned(ws, 256))
+      return fail(NVFP4DA_ERR_WORKSPACE, "shard front-half workspace too small (%zu < %zu bytes) or not 256-byte aligned",
+                  ws_bytes, bat_front_bytes(a));
+    p.xn = static_cast<uint16_t*>(ws);
+    p.rope_tab = reinterpret_cast<float2*>(static_cast<char*>(ws) + bat_rows_bytes(a));
+    e = launch_qkv_batched(p, hq + 2 * a->kv_heads, static_cast<cudaStream_t>(stream));
+  } else {
+    e = launch_qkv(p, pl, hq + 2 * a->kv_heads, static_cast<cudaStream_t>(stream), true);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "fused qkv launch");
   return NVFP4DA_OK;
 }

@@ -109,12 +109,16 @@ class CudaStages:
             a.output = q.data_ptr()
             a.batch, a.tokens, a.hidden, a.kv_heads, a.head_dim, a.capacity = b, t, h, hkv, d, shard.capacity
             a.past_lengths = None
+            # scratch of the batched front half (normalised rows, RoPE table), if the shape takes it
+            wsb = self.lib.nvfp4da_qkv_rope_append_shard_workspace_size(C.byref(a))
+            ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=x.device)
             # keep everything the struct points into alive with it
-            hit = self._bounded(self._front)[key] = (a, q, (x, g_in, g_q, g_k, k_shard, v_shard, wq, wk, wv))
-        a, q, _ = hit
+            hit = self._bounded(self._front)[key] = (a, q, (ws, wsb), (x, g_in, g_q, g_k, k_shard, v_shard, wq, wk, wv))
+        a, q, (ws, wsb), _ = hit
         a.past_length, a.max_past_length = past_length, past_length
         a.rms_eps, a.rope_theta = rms_eps, rope_theta
         st = self.lib.nvfp4da_qkv_rope_append_shard(C.byref(a), shard.start, global_capacity, q.data_ptr(),
+                                                    ws.data_ptr() if wsb else None, wsb,
                                                     torch.cuda.current_stream().cuda_stream)
         self.capi._check(st)
         return q

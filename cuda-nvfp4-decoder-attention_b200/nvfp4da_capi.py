@@ -26,7 +26,7 @@ EXPORTED = (
     "nvfp4da_gqa_attention_cached", "nvfp4da_forward_workspace_size", "nvfp4da_decoder_attention_forward",
     "nvfp4da_qkv_rope_append", "nvfp4da_decoder_attention_forward_noalloc",
     "nvfp4da_decoder_attention_forward_path", "nvfp4da_forward_step_supported", "nvfp4da_forward_sync_status",
-    "nvfp4da_debug_wait_timeout", "nvfp4da_qkv_rope_append_shard",
+    "nvfp4da_debug_wait_timeout", "nvfp4da_qkv_rope_append_shard", "nvfp4da_qkv_rope_append_shard_workspace_size",
     "nvfp4da_gqa_attention_partials_workspace_size", "nvfp4da_gqa_attention_partials",
     "nvfp4da_attention_combine", "nvfp4da_w4a16_gemm", "nvfp4da_decoder_attention_forward_hostio",
 )
@@ -95,7 +95,8 @@ def load() -> C.CDLL:
         "nvfp4da_forward_step_supported": (C.c_int, [C.POINTER(ForwardArgs)]),
         "nvfp4da_forward_sync_status": (C.c_int, [vp, C.POINTER(C.c_uint), C.c_int]),
         "nvfp4da_debug_wait_timeout": (C.c_int, [vp, C.c_ulonglong, C.POINTER(C.c_uint)]),
-        "nvfp4da_qkv_rope_append_shard": (C.c_int, [C.POINTER(ForwardArgs), i64, i64, vp, vp]),
+        "nvfp4da_qkv_rope_append_shard": (C.c_int, [C.POINTER(ForwardArgs), i64, i64, vp, vp, sz, vp]),
+        "nvfp4da_qkv_rope_append_shard_workspace_size": (sz, [C.POINTER(ForwardArgs)]),
         "nvfp4da_gqa_attention_partials_workspace_size": (sz, [i64, i64, i64, i64, i64, i64, i64, i64]),
         "nvfp4da_gqa_attention_partials": (C.c_int, [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, vp,
                                                      i64, vp, sz, vp]),

@@ -234,7 +234,12 @@ int nvfp4da_qkv_rope_append(const nvfp4da_forward_args* args, uint16_t* q_rope_o
  * shard's caches and args->capacity the shard capacity; positions are checked
  * against global_capacity; RoPE uses the global position. */
 int nvfp4da_qkv_rope_append_shard(const nvfp4da_forward_args* args, int64_t shard_start, int64_t global_capacity,
-                                  uint16_t* q_rope_out, void* stream);
+                                  uint16_t* q_rope_out, void* workspace, size_t workspace_bytes, void* stream);
+/* Workspace of nvfp4da_qkv_rope_append_shard (256-byte aligned): the
+ * normalised activation rows and RoPE table of the batched front half, used
+ * for 2..64 rows of D = 128; 0 where the shape takes the decode kernel (a
+ * NULL workspace is then accepted). */
+size_t nvfp4da_qkv_rope_append_shard_workspace_size(const nvfp4da_forward_args* args);
 /* Step 2: partials [B*T*Hq][D + 2] float32: o (unnormalised), m, l per query
  * row; a shard with no visible key gives m = -inf, l = 0, o = 0. */
 size_t nvfp4da_gqa_attention_partials_workspace_size(int64_t batch, int64_t tokens, int64_t q_heads,
