@@ -734,6 +734,80 @@ def run_attention_workload(args) -> None:
     _finish(world)
 
 
+def run_projections_workload(args) -> None:
+    """configs[2]'s projections alone (a separate line, not the default
+    workload): the batched front half (input RMSNorm + RoPE table, then Q/K/V
+    with per-head norm, RoPE and cache append in 4-CTA clusters) and the
+    batched O projection at M = 64 rows, each timed over 12 rotating weight
+    replicas (160 MB > L2).  Roofline: HBM bytes of weights and rows, and the
+    tensor FLOPs beside them."""
+    world, rank, local = dist_setup()
+    import nvfp4da_capi as capi
+    import synthetic
+
+    lib = capi.load()
+    b, h, hkv, d, cap = 64, 3072, 6, 128, 16
+    shape = synthetic.DecodeShape(batch=b, capacity=cap, past_lengths=tuple(i % cap for i in range(b)))
+    inp = synthetic.make_decode_inputs(shape, seed=5, cache_device="cuda")
+    x, g_in = inp.x.cuda(), inp.input_norm_weight.cuda()
+    g_q, g_k = inp.q_norm_weight.cuda(), inp.k_norm_weight.cuda()
+    ctx = torch.randn((b, h), generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).cuda()
+    y = torch.empty_like(ctx)
+    pl = torch.tensor(shape.past_lengths, dtype=torch.int64, device="cuda")
+    reps = []
+    for _ in range(12):
+        ws = _quantized_weights(inp, capi)
+        q = torch.empty((b, 1, h // d, d), dtype=torch.bfloat16, device="cuda")
+        fw = capi.Forward(x, g_in, ws["q"], ws["k"], ws["v"], g_q, g_k, ws["o"], inp.k_cache, inp.v_cache, y,
+                          past_length=0, past_lengths=pl, max_past_length=cap - 1)
+        wsb = lib.nvfp4da_qkv_rope_append_shard_workspace_size(C_byref(fw.args))
+        assert wsb > 0, "the batched front half does not cover configs[2]"
+        buf = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        reps.append((fw, ws, q, buf, wsb))
+    stream = torch.cuda.Stream()
+
+    def front():
+        for fw, _, q, buf, wsb in reps:
+            st = lib.nvfp4da_qkv_rope_append_shard(C_byref(fw.args), 0, cap, q.data_ptr(), buf.data_ptr(), wsb,
+                                                   stream.cuda_stream)
+            assert st == 0, lib.nvfp4da_last_error()
+
+    def oproj():
+        for _, ws, _, _, _ in reps:
+            capi.w4a16_linear(ctx, ws["o"], y, stream)
+
+    steps = max(3, min(args.steps, 200))
+    res = {}
+    for name, fn, n_out, k_rows in (("front", front, h + 2 * hkv * d, h), ("o_proj", oproj, h, h)):
+        ms, _ = _time_steps(fn, steps, max(args.warmup, 3), stream, world)
+        us = ms / (steps * len(reps)) * 1e3
+        byts = n_out * (k_rows // 2 + k_rows // 16) + 2 * b * k_rows * 2 + (b * 2 * hkv * d * 2 if name == "front" else 0)
+        fl = 2.0 * b * n_out * k_rows
+        res[name] = {"us": round(us, 3), "hbm_bytes": byts, "hbm_gbs": round(byts / (us * 1e-6) / 1e9, 1),
+                     "tflops": round(fl / (us * 1e-6) / 1e12, 1)}
+    peak, src = measured_peak_gbs()
+    tot_us = res["front"]["us"] + res["o_proj"]["us"]
+    tot_b = res["front"]["hbm_bytes"] + res["o_proj"]["hbm_bytes"]
+    ach = tot_b / (tot_us * 1e-6) / 1e9
+    if rank == 0:
+        print(json.dumps({"metric": "configs[2] batched projections us per step (M=64)", "value": round(tot_us, 3),
+                          "unit": "us", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+                          "higher_is_better": False, "dtype": "bf16 MMA on exact W4A16 products, fp32 accumulate",
+                          "data": "synthetic (seeded), 12 rotating weight replicas (160 MB > L2)",
+                          "config": {"workload": args.workload, "rows": b, "hidden": h},
+                          "kernels": res,
+                          "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                                       "frac": round(ach / peak, 4), "peak_source": src, "traffic": None}}),
+              flush=True)
+    _finish(world)
+
+
+def C_byref(obj):
+    import ctypes
+
+    return ctypes.byref(obj)
+
+
 def run_e2e_hostio(args, reps, stream, world) -> dict:
     """Same metric through the C ABI with host buffers: one library call per
     step copies a pinned host input in, runs the forward and copies the output
@@ -877,9 +951,11 @@ def main() -> None:
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-workloads", action="store_true",
                     help="only the configs[0] line (no configs[2]/[3]/[4] sub-objects)")
-    ap.add_argument("--workload", choices=("decode", "prefill", "attention-c3", "attention-c4"), default="decode",
+    ap.add_argument("--workload", choices=("decode", "prefill", "attention-c3", "attention-c4", "projections-c2"),
+                    default="decode",
                     help="decode = configs[0] (the metric's workload); prefill = configs[4], reported separately; "
-                         "attention-c3 / attention-c4 = one attention kernel on configs[3] / configs[4]")
+                         "attention-c3 / attention-c4 = one attention kernel on configs[3] / configs[4]; "
+                         "projections-c2 = the batched projections of configs[2] (M = 64)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -887,6 +963,8 @@ def main() -> None:
         run_prefill(args)
     elif args.workload.startswith("attention-"):
         run_attention_workload(args)
+    elif args.workload == "projections-c2":
+        run_projections_workload(args)
     else:
         run_gpu(args)
 

@@ -14,8 +14,8 @@
 //    K-quarter q of them, so each CTA reads only a quarter of the activation
 //    rows (every CTA reading whole rows made the activations' L2 lines the
 //    bottleneck: 144 CTAs x 384 KB at M = 64);
-//  * at launch, before the programmatic-dependency wait, the CTA bulk-copies
-//    its 128 x K/4 weight block and its scale block into shared memory; after
+//  * at launch, before the programmatic-dependency wait, the CTA copies its
+//    128 x K/4 weight block and its scale block into shared memory; after
 //    the wait, its K-quarter of every activation row (row stride K/2 + 32
 //    bytes, so the 16-byte operand loads of a warp hit distinct banks);
 //  * warp w takes tiles 2 (w % 4) and 2 (w % 4) + 1 (32 weight rows) and the
@@ -39,6 +39,7 @@
 
 #include <cooperative_groups.h>
 
+#include "attention_prefill.cuh"  // cp_async16
 #include "elementwise.cuh"
 #include "gemv_kernel.cuh"
 #include "gemv_mma.cuh"
@@ -80,43 +81,51 @@ __host__ __device__ inline bool bat_shape_ok(int64_t m, int64_t n, int64_t k) {
   return m >= kBatMinM && m <= kBatMaxM && k >= 1024 && k % 1024 == 0 && n % kBatRows == 0;
 }
 
-// Warp 0: bulk-copy the CTA's scale and weight blocks (rows row0 ..
-// row0 + 127, K-quarter q) with completion on `bar`.
+// The CTA's blocks are strided in global memory (a K-quarter of each row),
+// so they are staged with 16-byte asynchronous copies from every thread:
+// hundreds of small bulk copies per CTA measured several microseconds of
+// issue time alone.
+__device__ __forceinline__ void bat_cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bat_cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// All threads: copy the CTA's scale and weight blocks (rows row0 .. row0 +
+// 127, K-quarter q) and commit them as one group.
 __device__ __forceinline__ void bat_stage_weights(uint8_t* smem, const uint8_t* scales, const uint8_t* packed,
-                                                  int64_t row0, int64_t k, int q, uint64_t* bar) {
-  const int lane = threadIdx.x & 31;
+                                                  int64_t row0, int64_t k, int q) {
   const int64_t kq = bat_quarter(k);
-  const uint32_t sb = static_cast<uint32_t>(kq / 16), wb = static_cast<uint32_t>(kq / 2);
-  if (lane == 0) mbar_arrive_expect_tx(bar, kBatRows * (sb + wb));
-  __syncwarp();
-  for (int r = lane; r < kBatRows; r += 32) {
-    bulk_g2s(smem + r * sb, scales + (row0 + r) * (k / 16) + q * sb, sb, bar);
-    bulk_g2s(smem + bat_scale_bytes(k) + r * wb, packed + (row0 + r) * (k / 2) + q * wb, wb, bar);
+  const int sc = static_cast<int>(kq / 256), wc = static_cast<int>(kq / 32);  // 16-byte chunks per row
+  const uint32_t sbase = smem_u32(smem), wbase = smem_u32(smem + bat_scale_bytes(k));
+  for (int i = threadIdx.x; i < kBatRows * sc; i += kBatThreads) {
+    const int r = i / sc, c = i % sc;
+    cp_async16(sbase + r * sc * 16 + c * 16, scales + (row0 + r) * (k / 16) + q * (kq / 16) + c * 16, true);
   }
+  for (int i = threadIdx.x; i < kBatRows * wc; i += kBatThreads) {
+    const int r = i / wc, c = i % wc;
+    cp_async16(wbase + r * wc * 16 + c * 16, packed + (row0 + r) * (k / 2) + q * (kq / 2) + c * 16, true);
+  }
+  bat_cp_async_commit();
 }
 
-// Warp 0: bulk-copy K-quarter q of activation rows [0, m) (completion on `bar`).
-__device__ __forceinline__ void bat_stage_rows(uint8_t* dst, const uint16_t* xrows, int64_t k, int m, int q,
-                                               uint64_t* bar) {
-  const int lane = threadIdx.x & 31;
+// All threads: copy K-quarter q of activation rows [0, m) and commit.
+__device__ __forceinline__ void bat_stage_rows(uint8_t* dst, const uint16_t* xrows, int64_t k, int m, int q) {
   const int64_t kq = bat_quarter(k);
-  const uint32_t bytes = static_cast<uint32_t>(kq * 2);
-  if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(m) * bytes);
-  __syncwarp();
-  for (int r = lane; r < m; r += 32)
-    bulk_g2s(dst + r * bat_row_stride(k), xrows + static_cast<int64_t>(r) * k + q * kq, bytes, bar);
+  const int xc = static_cast<int>(kq / 8);
+  const uint32_t base = smem_u32(dst), rs = bat_row_stride(k);
+  for (int i = threadIdx.x; i < m * xc; i += kBatThreads) {
+    const int r = i / xc, c = i % xc;
+    cp_async16(base + r * rs + c * 16, xrows + static_cast<int64_t>(r) * k + q * kq + c * 8, true);
+  }
+  bat_cp_async_commit();
 }
 
 // The cluster's 128 rows x M outputs: CTA q returns rows [32 q, 32 q + 32)
 // (before gamma) as [32][MP] FP32 in its own shared memory (the pointer
 // returned).  All threads of every CTA of the cluster call it after the
-// programmatic-dependency wait; the weight copies were issued on `wbar`
-// before it.  Bounded waits: a timeout is recorded in *err (when given) and
-// the pass carries on with whatever the buffers hold.  After it returns no
-// CTA touches another's shared memory.
+// programmatic-dependency wait; the weight copies were issued
+// (bat_stage_weights) before it.  After it returns no CTA touches another's
+// shared memory.
 template <int NT, unsigned PHASE_BASE>
-__device__ __forceinline__ const float* bat_pass(uint8_t* smem, uint64_t* wbar, uint64_t* xbar, const uint16_t* xrows,
-                                                 int64_t k, int m, unsigned* err) {
+__device__ __forceinline__ const float* bat_pass(uint8_t* smem, const uint16_t* xrows, int64_t k, int m) {
   [[maybe_unused]] constexpr unsigned kPhaseBase = PHASE_BASE;
   constexpr int MP = NT * 8;
   namespace cg = cooperative_groups;
@@ -130,7 +139,7 @@ __device__ __forceinline__ const float* bat_pass(uint8_t* smem, uint64_t* wbar, 
   const uint8_t* s_smem = smem;
   const uint8_t* w_smem = smem + bat_scale_bytes(k);
   uint8_t* act = smem + bat_act_off(k);
-  if (warp == 0) bat_stage_rows(act, xrows, k, m, q, xbar);
+  bat_stage_rows(act, xrows, k, m, q);
   // lane's bytes: rows 32 tp + g + 8 r (r = 0..3: tiles 2 tp, 2 tp + 1, lower / upper half)
   const uint8_t* wl0 = w_smem + (32 * tp + g) * kb + 16 * t;
   const uint8_t* sc0 = s_smem + (32 * tp + g) * ks + 2 * t;
@@ -142,9 +151,9 @@ __device__ __forceinline__ const float* bat_pass(uint8_t* smem, uint64_t* wbar, 
   for (int tl = 0; tl < 2; ++tl)
 #pragma unroll
     for (int n = 0; n < NT; ++n) d[tl][n][0] = d[tl][n][1] = d[tl][n][2] = d[tl][n][3] = 0.0f;
-  mbar_wait_bounded(wbar, 0, err);
   NVFP4DA_PHASE(3);
-  mbar_wait_bounded(xbar, 0, err);
+  bat_cp_async_wait_all();
+  __syncthreads();  // every thread's copies have landed
   NVFP4DA_PHASE(4);
   for (int s = sh; s < steps; s += 2) {
     uint4 wv[4];
@@ -324,7 +333,6 @@ __global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThread
   constexpr int MP = NT * 8;
   constexpr int D = kBatRows;  // one head per cluster
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t wbar, xbar;
   __shared__ __align__(16) uint16_t head_out[MP][D];
   [[maybe_unused]] constexpr unsigned kPhaseBase = 0;
   NVFP4DA_PHASE(0);
@@ -351,13 +359,7 @@ __global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThread
   }
   const int64_t row0 = head * D;
 
-  if (threadIdx.x == 0) {
-    mbar_init(&wbar, 1);
-    mbar_init(&xbar, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();  // the barriers are initialised
-  if (warp == 0) bat_stage_weights(smem, p.scales[mat], p.packed[mat], row0, k, rank, &wbar);
+  bat_stage_weights(smem, p.scales[mat], p.packed[mat], row0, k, rank);
   const float gamma = *p.gamma[mat];
   NVFP4DA_PHASE(1);
 
@@ -365,7 +367,7 @@ __global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThread
   NVFP4DA_PHASE(2);
   if (blockIdx.x == 0)
     for (int64_t i = threadIdx.x; i < p.n_zero_words; i += blockDim.x) p.zero_words[i] = 0u;
-  const float* outv = bat_pass<NT, 0>(smem, &wbar, &xbar, p.xn, k, m, p.err);
+  const float* outv = bat_pass<NT, 0>(smem, p.xn, k, m);
 
   uint16_t* leader_out = cluster.map_shared_rank(&head_out[0][0], 0);
   for (int i = threadIdx.x; i < kBatRowsPerCta * m; i += kBatThreads) {
@@ -443,7 +445,6 @@ __global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThread
     o_batched_kernel(const __grid_constant__ GemvParams p) {
   constexpr int MP = NT * 8;
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t wbar, xbar;
   namespace cg = cooperative_groups;
   const int rank = static_cast<int>(cg::this_cluster().block_rank());
   const int64_t k = p.k;
@@ -451,13 +452,7 @@ __global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThread
   const int64_t row0 = static_cast<int64_t>(blockIdx.x / kBatCluster) * kBatRows;
   [[maybe_unused]] constexpr unsigned kPhaseBase = 2048;
   NVFP4DA_PHASE(0);
-  if (threadIdx.x == 0) {
-    mbar_init(&wbar, 1);
-    mbar_init(&xbar, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if ((threadIdx.x >> 5) == 0) bat_stage_weights(smem, p.scales, p.packed, row0, k, rank, &wbar);
+  bat_stage_weights(smem, p.scales, p.packed, row0, k, rank);
   const float gamma = *p.gamma;
   NVFP4DA_PHASE(1);
   if (p.pdl) {
@@ -465,7 +460,7 @@ __global__ void __cluster_dims__(kBatCluster, 1, 1) __launch_bounds__(kBatThread
     pdl_launch_dependents();
   }
   NVFP4DA_PHASE(2);
-  const float* outv = bat_pass<NT, 2048>(smem, &wbar, &xbar, p.x, k, m, p.err);
+  const float* outv = bat_pass<NT, 2048>(smem, p.x, k, m);
   const int64_t r0 = row0 + rank * kBatRowsPerCta;
   for (int i = threadIdx.x; i < kBatRowsPerCta * m; i += kBatThreads) {
     const int n = i / kBatRowsPerCta, r = i % kBatRowsPerCta;
