@@ -78,16 +78,29 @@ def step_bytes(shape) -> dict:
     return {"qkv": qkv, "attention": attn, "o_proj": o, "step": total}
 
 
-def kernel_source_digest() -> str:
-    """First 16 hex digits of the SHA-256 over the kernel sources (every
-    csrc/*.cuh, in name order): a profile captured from other sources no
-    longer describes the kernels that run."""
-    import hashlib
+KERNEL_HEADERS = {"decode_step": "decode_step.cuh", "qkv_fused": "qkv_fused.cuh", "attn_stream": "attention_stream.cuh",
+                  "qkv_batched": "gemv_batched.cuh", "o_batched": "gemv_batched.cuh"}
 
+
+def kernel_source_digest(header: str) -> str:
+    """First 16 hex digits of the SHA-256 over a kernel's header and every
+    header it includes from csrc/ (transitively, in name order): a profile
+    captured from other sources no longer describes the kernel that runs."""
+    import hashlib
+    import re
+
+    csrc = PKG / "csrc"
+    seen, todo = set(), [header]
+    while todo:
+        f = todo.pop()
+        if f in seen or not (csrc / f).is_file():
+            continue
+        seen.add(f)
+        todo += re.findall(r'#include "([^"/]+)"', (csrc / f).read_text())
     h = hashlib.sha256()
-    for f in sorted((PKG / "csrc").glob("*.cuh")):
-        h.update(f.name.encode())
-        h.update(f.read_bytes())
+    for f in sorted(seen):
+        h.update(f.encode())
+        h.update((csrc / f).read_bytes())
     return h.hexdigest()[:16]
 
 
@@ -95,8 +108,8 @@ def ncu_traffic(kernel: str, summary: str | None = None) -> float | None:
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
     summary (profiles/<kernel>_canonical.md, or profiles/<summary>, line
     `dram_bytes_per_launch: N`), or None when the summary's
-    `kernel_sources: <digest>` line does not match the kernel sources of this
-    tree (the capture predates a kernel change)."""
+    `kernel_sources: <digest>` line does not match kernel_source_digest of the
+    kernel's header in this tree (the capture predates a kernel change)."""
     import re
 
     p = ROOT / "profiles" / (summary or f"{kernel}_canonical.md")
@@ -105,10 +118,10 @@ def ncu_traffic(kernel: str, summary: str | None = None) -> float | None:
     except OSError:
         return None
     src = re.search(r"kernel_sources:\s*([0-9a-f]+)", text)
-    if not src or src.group(1) != kernel_source_digest():
+    if not src or src.group(1) != kernel_source_digest(KERNEL_HEADERS[kernel]):
         return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", text)
-    return float(m.group(1)) if m else None
+    m = re.findall(r"^dram_bytes_per_launch:\s*([0-9.eE+]+)", text, re.M)  # the latest capture: the last line
+    return float(m[-1]) if m else None
 
 
 def measured_peak_gbs() -> tuple[float, str]:
