@@ -779,7 +779,8 @@ bool step_covers(const nvfp4da_forward_args* a);  // the one-kernel step plans t
 bool bat_front_ok(const nvfp4da_forward_args* a) {
   const int64_t m = a->batch * a->tokens;
   return a->head_dim == kBatRows && bat_shape_ok(m, a->hidden, a->hidden) && a->hidden <= 64 * kNormThreads &&
-         bat_smem_bytes(a->hidden, 64) <= kMaxDynSmem && aligned(a->x, 16) && aligned(a->input_norm_weight, 16) &&
+         bat_smem_bytes(a->hidden, 64) + kBatMaxM * kBatRows * 2 <= kMaxDynSmem &&  // + the static head rows
+         aligned(a->x, 16) && aligned(a->input_norm_weight, 16) &&
          !(a->stages && a->stages->input_normalized && !aligned(a->stages->input_normalized, 16)) &&
          bat_weights_aligned(a);
 }

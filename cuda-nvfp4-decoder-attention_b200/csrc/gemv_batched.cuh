@@ -55,14 +55,20 @@ constexpr int kBatRowsPerCta = kBatRows / kBatCluster;
 constexpr int kBatThreads = 256;
 
 // Dynamic shared memory of one CTA (K-quarter kq = K / 4): scales [128][kq/16],
-// weights [128][kq/2], the activation rows [MP][kq * 2 + 32 bytes] (which the
+// weights [128][kq/2, row stride bat_wrow_stride], the activation rows [MP][kq * 2 + 32 bytes] (which the
 // step-half partials [128][MP] FP32 and then the CTA's results [32][MP]
 // overlay once the MMAs are done), and the inbox [4 quarters][32][MP] FP32
 // that the cluster's CTAs write their partials of this CTA's rows into.
 __host__ __device__ inline int64_t bat_quarter(int64_t k) { return k / kBatCluster; }
 __host__ __device__ inline uint32_t bat_row_stride(int64_t k) { return static_cast<uint32_t>(bat_quarter(k) * 2 + 32); }
 __host__ __device__ inline uint32_t bat_scale_bytes(int64_t k) { return static_cast<uint32_t>(kBatRows * (bat_quarter(k) / 16)); }
-__host__ __device__ inline uint32_t bat_weight_bytes(int64_t k) { return static_cast<uint32_t>(kBatRows * (bat_quarter(k) / 2)); }
+// Staged weight rows: K/8 bytes, padded to 64 mod 128 so that the two rows
+// a quarter-warp reads at once (g, g + 1) fall in different banks.
+__host__ __device__ inline uint32_t bat_wrow_stride(int64_t k) {
+  const uint32_t kb = static_cast<uint32_t>(bat_quarter(k) / 2);
+  return kb + ((64u - kb % 128u) + 128u) % 128u;
+}
+__host__ __device__ inline uint32_t bat_weight_bytes(int64_t k) { return kBatRows * bat_wrow_stride(k); }
 __host__ __device__ inline uint32_t bat_act_off(int64_t k) { return bat_scale_bytes(k) + bat_weight_bytes(k); }
 __host__ __device__ inline uint32_t bat_act_bytes(int64_t k, int mpad) {
   const uint32_t rows = static_cast<uint32_t>(mpad) * bat_row_stride(k);
@@ -94,14 +100,14 @@ __device__ __forceinline__ void bat_stage_weights(uint8_t* smem, const uint8_t* 
                                                   int64_t row0, int64_t k, int q) {
   const int64_t kq = bat_quarter(k);
   const int sc = static_cast<int>(kq / 256), wc = static_cast<int>(kq / 32);  // 16-byte chunks per row
-  const uint32_t sbase = smem_u32(smem), wbase = smem_u32(smem + bat_scale_bytes(k));
+  const uint32_t sbase = smem_u32(smem), wbase = smem_u32(smem + bat_scale_bytes(k)), ws = bat_wrow_stride(k);
   for (int i = threadIdx.x; i < kBatRows * sc; i += kBatThreads) {
     const int r = i / sc, c = i % sc;
     cp_async16(sbase + r * sc * 16 + c * 16, scales + (row0 + r) * (k / 16) + q * (kq / 16) + c * 16, true);
   }
   for (int i = threadIdx.x; i < kBatRows * wc; i += kBatThreads) {
     const int r = i / wc, c = i % wc;
-    cp_async16(wbase + r * wc * 16 + c * 16, packed + (row0 + r) * (k / 2) + q * (kq / 2) + c * 16, true);
+    cp_async16(wbase + r * ws + c * 16, packed + (row0 + r) * (k / 2) + q * (kq / 2) + c * 16, true);
   }
   bat_cp_async_commit();
 }
@@ -135,7 +141,7 @@ __device__ __forceinline__ const float* bat_pass(uint8_t* smem, const uint16_t* 
   const int tp = warp & 3, sh = warp >> 2;  // tile pair, step parity
   const int64_t kq = bat_quarter(k);
   const int steps = static_cast<int>(kq / 128);
-  const uint32_t ks = static_cast<uint32_t>(kq / 16), kb = static_cast<uint32_t>(kq / 2), rs = bat_row_stride(k);
+  const uint32_t ks = static_cast<uint32_t>(kq / 16), kb = bat_wrow_stride(k), rs = bat_row_stride(k);
   const uint8_t* s_smem = smem;
   const uint8_t* w_smem = smem + bat_scale_bytes(k);
   uint8_t* act = smem + bat_act_off(k);
