@@ -700,6 +700,8 @@ def run_attention_workload(args) -> None:
     c3 = args.workload == "attention-c3"
     b, t, hq, hkv, d = (8, 1, 24, 6, 128) if c3 else (4, 2048, 24, 6, 128)
     cap, past = (32768, 32767) if c3 else (4096, 0)
+    if c3 and args.positions:  # a shorter cache of the same shape (profiling captures)
+        cap, past = args.positions, args.positions - 1
     g = torch.Generator(device="cuda").manual_seed(1)
     q = torch.randn((b, t, hq, d), generator=g, device="cuda").to(torch.bfloat16)
     k = torch.randn((b, hkv, cap, d), generator=g, device="cuda").to(torch.bfloat16)
@@ -723,7 +725,7 @@ def run_attention_workload(args) -> None:
         ach = byts / (ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
                 "peak_source": src, "bytes_per_launch": byts,
-                "traffic": ncu_traffic("attn_stream", "attn_stream_configs3.md"),
+                "traffic": None if args.positions else ncu_traffic("attn_stream", "attn_stream_configs3.md"),
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
                                   "(profiles/attn_stream_configs3.md)"}
         metric, value, unit = "configs[3] decode attention HBM GB/s", round(ach, 1), "GB/s"
@@ -743,7 +745,8 @@ def run_attention_workload(args) -> None:
         print(json.dumps({"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
                           "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
                           "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v)",
-                          "config": {"workload": args.workload}, "roofline": roof}), flush=True)
+                          "config": {"workload": args.workload, "capacity": cap, "past_length": past},
+                          "roofline": roof}), flush=True)
     _finish(world)
 
 
@@ -969,6 +972,8 @@ def main() -> None:
                     help="decode = configs[0] (the metric's workload); prefill = configs[4], reported separately; "
                          "attention-c3 / attention-c4 = one attention kernel on configs[3] / configs[4]; "
                          "projections-c2 = the batched projections of configs[2] (M = 64)")
+    ap.add_argument("--positions", type=int, default=0,
+                    help="attention-c3 only: cache positions per sequence (default 32768, the config's)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -18,10 +18,13 @@
 // of a pair to finish -- an atomic counter, no waiting -- combines its pair's
 // partials in CTA order.
 //
-// Per CTA: warp 4 (one lane) issues the TMA loads of K and V tiles (64 rows x
+// Per CTA: warp 8 (one lane) issues the TMA loads of K and V tiles (64 rows x
 // 64 elements per box, 128-byte swizzle, so ldmatrix reads are conflict-free)
 // into a ring of kStages stages, running ahead across segment boundaries;
-// warps 0-3 take 16 positions of every tile each.  One KV head's queries
+// two groups of four consumer warps take alternate tiles (the CTA's n-th tile
+// goes to group n % 2), each warp 16 positions of its group's tiles.  With
+// one group the per-tile dependency chain (S^T MMAs, softmax, PV MMAs) set
+// the pace below the HBM rate.  One KV head's queries
 // (group x T <= 8 rows) are the N = 8 side of the tensor-core tiles:
 //   S^T[pos, q]  = K[pos, :] . Q^T      mma.m16n8k16, BF16 x BF16 -> FP32
 //   O^T[d, q]   += V^T[d, pos] P^T      P split as BF16 hi + lo (two MMAs),
@@ -45,7 +48,8 @@
 namespace nvfp4da {
 
 constexpr int kAsTile = 64;            // positions per stage
-constexpr int kAsConsumerWarps = 4;    // 16 positions of every tile each
+constexpr int kAsGroupWarps = 4;       // 16 positions of a tile each
+constexpr int kAsConsumerWarps = 8;    // two groups, alternate tiles
 constexpr int kAsThreads = (kAsConsumerWarps + 1) * 32;
 constexpr int kAsRows = 8;             // query rows per KV head (the MMA's N)
 constexpr uint32_t kAsBox = kAsTile * 128;  // one 64-row x 64-element box: 8 KB
@@ -60,7 +64,13 @@ struct AsCfg {
   // Stages in flight: what is left of 217 KB after the combine area (the
   // rest holds the alignment slack and up to kAsMaxBatch sequences' prefix).
   static constexpr int kStagesFit = static_cast<int>((217u * 1024 - kComb) / kStage);
-  static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;  // 12, 6 or 2
+  // An even count: the CTA's n-th tile goes to stage n % kStages and consumer
+  // group n % 2, so every stage serves one group only.  (With an odd count a
+  // group one ring ahead of the other would wait on a stage whose previous
+  // phase -- the other group's tile, still landing -- already reads as
+  // complete: the parity wait cannot tell the two apart.)
+  static constexpr int kStages = (kStagesFit > 12 ? 12 : kStagesFit) & ~1;  // 12, 4 or 2
+  static_assert(kStages >= 2, "two stages at least");
   static constexpr uint32_t kRing = kStages * kStage;
   // ring (1024-aligned) + combine + m/l + barriers; the per-sequence tile
   // prefix (int64 [B + 1]) follows.
@@ -186,7 +196,7 @@ __global__ void __launch_bounds__(kAsThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kAsConsumerWarps);
+      mbar_init(&empty[s], kAsGroupWarps);
     }
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_k)) : "memory");
@@ -282,11 +292,11 @@ __global__ void __launch_bounds__(kAsThreads, 1)
   // ------------------------------------------------------------------ consumers
   if (p.pdl) pdl_wait();  // q comes from the kernel before this one
   const int g = lane >> 2, tq = lane & 3;  // fragment row group / column pair
+  const int grp = warp / kAsGroupWarps, wq = warp % kAsGroupWarps;
   AsWalk w;
   bool more = w.begin(prefix, p.batch, hkv, x0, x1);
   bool dead = false;
-  int stage = 0;
-  uint32_t phase = 0;
+  long long it = 0;  // the CTA's tile counter, as the producer counts
   while (more) {
     const int b = w.b, kvh = w.kvh;
     const int64_t pb = p.past_lengths ? p.past_lengths[b] : p.past_length;
@@ -317,11 +327,14 @@ __global__ void __launch_bounds__(kAsThreads, 1)
 #pragma unroll
     for (int i = 0; i < KS; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
 
-    for (int t = w.t0; t < w.t1; ++t) {
+    for (int t = w.t0; t < w.t1; ++t, ++it) {
+      if ((it & 1) != grp) continue;
+      const int stage = static_cast<int>(it % Cfg::kStages);
+      const uint32_t phase = static_cast<uint32_t>(it / Cfg::kStages) & 1u;
       if (!dead && !mbar_wait_bounded(&full[stage], phase, p.err)) dead = true;
       const uint8_t* kt = smem + stage * Cfg::kStage;
       const uint8_t* vt = kt + Cfg::kBoxes * kAsBox;
-      const int64_t pos0 = static_cast<int64_t>(t) * kAsTile + warp * 16;  // this warp's first position
+      const int64_t pos0 = static_cast<int64_t>(t) * kAsTile + wq * 16;  // this warp's first position
       if (!dead && pos0 < vis) {
         if (pos0 + 16 > vis) {
           // The sequence ends inside this warp's rows: rows at or past it may
@@ -331,7 +344,7 @@ __global__ void __launch_bounds__(kAsThreads, 1)
             const int r = i / (Cfg::kBoxes * 8);
             if (pos0 + r >= vis) {
               const int bx = (i / 8) % Cfg::kBoxes, c = i % 8;
-              *reinterpret_cast<uint4*>(const_cast<uint8_t*>(vt) + bx * kAsBox + (warp * 16 + r) * 128 + c * 16) =
+              *reinterpret_cast<uint4*>(const_cast<uint8_t*>(vt) + bx * kAsBox + (wq * 16 + r) * 128 + c * 16) =
                   make_uint4(0u, 0u, 0u, 0u);
             }
           }
@@ -341,7 +354,7 @@ __global__ void __launch_bounds__(kAsThreads, 1)
         // ---- S^T = K Q^T for this warp's 16 positions (two accumulators)
         float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
         {
-          const int mat = lane >> 3, r = warp * 16 + (mat & 1) * 8 + (lane & 7);
+          const int mat = lane >> 3, r = wq * 16 + (mat & 1) * 8 + (lane & 7);
           const uint32_t rbase = smem_u32(kt) + r * 128;
 #pragma unroll
           for (int ks = 0; ks < KS; ++ks) {
@@ -389,7 +402,7 @@ __global__ void __launch_bounds__(kAsThreads, 1)
         const uint32_t bl0 = movmatrix_trans(l01), bl1 = movmatrix_trans(l23);
         // ---- O^T += V^T P^T
         {
-          const int mat = lane >> 3, r = warp * 16 + (mat >> 1) * 8 + (lane & 7);
+          const int mat = lane >> 3, r = wq * 16 + (mat >> 1) * 8 + (lane & 7);
           const uint32_t rbase = smem_u32(vt) + r * 128;
 #pragma unroll
           for (int mt = 0; mt < KS; ++mt) {
@@ -403,13 +416,9 @@ __global__ void __launch_bounds__(kAsThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == Cfg::kStages) {
-        stage = 0;
-        phase ^= 1u;
-      }
     }
 
-    // ---- this segment's (m, l, o): combine the four warps
+    // ---- this segment's (m, l, o): combine the eight warps
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       l_run[c] += __shfl_xor_sync(kFull, l_run[c], 4);
