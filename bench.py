@@ -117,11 +117,18 @@ def ncu_traffic(kernel: str, summary: str | None = None) -> float | None:
         text = p.read_text()
     except OSError:
         return None
-    src = re.search(r"kernel_sources:\s*([0-9a-f]+)", text)
-    if not src or src.group(1) != kernel_source_digest(KERNEL_HEADERS[kernel]):
-        return None
-    m = re.findall(r"^dram_bytes_per_launch:\s*([0-9.eE+]+)", text, re.M)  # the latest capture: the last line
-    return float(m[-1]) if m else None
+    # The capture that describes this tree: the `dram_bytes_per_launch` line
+    # last seen before a `kernel_sources` line whose digest matches.
+    want = kernel_source_digest(KERNEL_HEADERS[kernel])
+    last = None
+    for line in text.splitlines():
+        m = re.match(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", line)
+        if m:
+            last = float(m.group(1))
+        m = re.match(r"kernel_sources:\s*([0-9a-f]+)", line)
+        if m and m.group(1) == want:
+            return last
+    return None
 
 
 def measured_peak_gbs() -> tuple[float, str]:
